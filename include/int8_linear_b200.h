@@ -1,0 +1,169 @@
+/*
+ * int8_linear_b200.h - C ABI of the B200 (sm_100a) W8A8 linear-layer library.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes and a
+ * CUDA stream handle (a cudaStream_t passed as void*; NULL is the legacy default
+ * stream).  Nothing here allocates device memory: the caller owns every buffer,
+ * including the split-K workspace.  Calls are asynchronous on the given stream and
+ * never synchronise the host.
+ *
+ * Return codes: I8L_OK, or one of the I8L_E* codes; i8l_last_error() gives a
+ * one-line message for the calling host thread.  I8L_ENOTSUP means "this kernel
+ * does not take that shape/dtype/layout; the caller should fall back"; it maps to
+ * int8_linear.NotSupported in the Python layer.  I8L_EINVAL maps to ValueError.
+ *
+ * The reference (AshrithaG/int8-linear) is a Python/Triton package with no native
+ * ABI; each entry below replaces the Triton launch of one reference function, cited
+ * by file:line inside that project.
+ */
+#ifndef INT8_LINEAR_B200_H
+#define INT8_LINEAR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ---------------------------------------------------------- */
+#define I8L_OK 0
+#define I8L_ENOTSUP 1   /* shape/dtype/layout the kernel declines (NotSupported)   */
+#define I8L_EINVAL 2    /* inconsistent arguments (ValueError)                     */
+#define I8L_ECUDA 3     /* a CUDA runtime/driver call failed (RuntimeError)        */
+#define I8L_EWORKSPACE 4 /* workspace missing or smaller than i8l_workspace_size() */
+
+/* ---- element type codes ---------------------------------------------------- */
+#define I8L_BF16 0
+#define I8L_F16 1
+#define I8L_F32 2
+#define I8L_I32 3 /* GEMM output only: the raw int32 product (reference raw=True) */
+
+/* ---- GEMM tile selection ---------------------------------------------------- */
+/*
+ * One GEMM tile configuration.  A zero-initialised struct (or a NULL pointer)
+ * asks the library for its own choice.
+ *   swap_ab = 1: the weight rows fill the 128-row MMA M side and the tokens are the
+ *                MMA N side, tok_tile in {16,32,64,128,256} (decode shapes);
+ *   swap_ab = 0: tokens fill the 128-row MMA M side, w_tile in {128,256}.
+ *   stages:      shared-memory ring depth (0 = the most that fits);
+ *   ctas:        persistent CTAs (0 = one per SM);
+ *   group:       tiles walked together along the 128-row side for L2 reuse (>=1);
+ *   split:       0 = stream-K over the SMs (tiles may be split along K and the int32
+ *                partial sums reduced exactly through the workspace), 1 = whole tiles.
+ */
+typedef struct i8l_tile {
+  int32_t swap_ab;
+  int32_t tok_tile;
+  int32_t w_tile;
+  int32_t stages;
+  int32_t ctas;
+  int32_t group;
+  int32_t split;
+  int32_t reserved;
+} i8l_tile;
+
+/*
+ * out[M,N] = (A[M,K] @ W[N,K]^T) * sa * sb + bias, int8 x int8 -> int32 on the
+ * tcgen05 tensor cores, dequantised in fp32 in the epilogue and rounded once to the
+ * output type.  With out_dtype == I8L_I32 the exact int32 product is stored and
+ * sa/sb/bias are ignored.
+ *
+ *   A   int8, row m at A + m*lda  (K contiguous); lda*1 and A must be 16-byte aligned
+ *   W   int8, row n at W + n*ldw  (K contiguous); this is the [K,N] view b_q with
+ *       strides (1, ldw) that the reference takes; 16-byte alignment as for A
+ *   sa  float32, M values (sa_per_row=1) or one value
+ *   sb  float32, N values (sb_per_col=1) or one value
+ *   bias NULL or N values of bias_dtype (I8L_BF16/I8L_F16/I8L_F32)
+ *   out row m at out + m*ldc elements of out_dtype (I8L_BF16/F16/F32/I32)
+ *   K must be a positive multiple of 16.
+ *   workspace/ws_bytes: at least i8l_workspace_size(...) bytes, zero-filled by the
+ *       caller ONCE when first allocated; every call leaves it zero-filled again.
+ *       Calls that share a workspace must not overlap on the GPU.
+ *
+ * Replaces the reference's launcher w8a8_mm (int8_linear/kernel.py:202-257) and
+ * its Triton kernel _w8a8_mm (int8_linear/kernel.py:63-124).
+ */
+int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
+                const float *sa, int32_t sa_per_row, const float *sb,
+                int32_t sb_per_col, const void *bias, int32_t bias_dtype,
+                void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
+                int32_t K, const i8l_tile *tile, void *workspace,
+                size_t ws_bytes, void *stream);
+
+/*
+ * Bytes of workspace i8l_w8a8_mm needs for this problem and tile (tile may be
+ * NULL for the library's choice).  Host-only, no CUDA calls beyond a cached
+ * device-property query.  Replaces nothing in the reference (Triton's kernel kept
+ * no cross-CTA state); the workspace exists for the exact int32 split-K reduction.
+ */
+size_t i8l_workspace_size(int32_t M, int32_t N, int32_t K, const i8l_tile *tile);
+
+/*
+ * The tile the library picks when none is given (the untuned heuristic).
+ * Replaces default_config (int8_linear/kernel.py:127-134).
+ */
+int i8l_default_tile(int32_t M, int32_t N, int32_t K, i8l_tile *tile_out);
+
+/*
+ * add + RMSNorm + per-token int8 quantisation, one token row per CTA:
+ *   x' = x (+ residual) in fp32; rout = x' rounded to act_dtype (if residual);
+ *   var = sum(x'^2)/K; xn = x' * rsqrt(var + eps);
+ *   y = act(w_dtype(xn) * weight); scale = max|y|/127; q = rint(y*127/max|y|).
+ * x, residual, rout: act_dtype (I8L_BF16 or I8L_F16), rows at ld* elements.
+ * weight: K values of w_dtype (I8L_BF16/F16/F32).  residual/rout may be NULL
+ * together.  q: int8 rows at ldq; scale: M float32.
+ * Replaces add_rmsnorm_quant (int8_linear/fused_quant.py:95-110) and its kernel
+ * _add_rmsnorm_quant_kernel (int8_linear/fused_quant.py:56-73) with the row
+ * quantiser _quantize_row (int8_linear/fused_quant.py:41-53).
+ */
+int i8l_add_rmsnorm_quant(const void *x, int64_t ldx, const void *residual,
+                          int64_t ldr, const void *weight, int32_t act_dtype,
+                          int32_t w_dtype, int8_t *q, int64_t ldq, float *scale,
+                          void *rout, int64_t ldro, int32_t M, int32_t K,
+                          float eps, int32_t precise_div, void *stream);
+
+/*
+ * SiLU-and-mul + per-token int8 quantisation: gate = row[0:I], up = row[I:2I];
+ *   a = g/(1+exp(-g)); a rounded to act_dtype if round_silu; y = act(a*u);
+ *   then the row quantiser as above.
+ * gate_up: act_dtype rows of 2I elements at ld; q: int8 rows at ldq; scale: M f32.
+ * Replaces silu_mul_quant (int8_linear/fused_quant.py:113-124) and
+ * _silu_mul_quant_kernel (int8_linear/fused_quant.py:76-88).
+ */
+int i8l_silu_mul_quant(const void *gate_up, int64_t ld, int32_t act_dtype,
+                       int8_t *q, int64_t ldq, float *scale, int32_t M,
+                       int32_t I, int32_t precise_div, int32_t round_silu,
+                       void *stream);
+
+/*
+ * Plain dynamic per-token int8 quantisation of an act_dtype [M,K] matrix (rows at
+ * ldx elements, so a column slice of a wider matrix needs no copy).  The same
+ * row quantiser as above.  The reference reaches this step through vLLM's
+ * scaled_int8_quant (called in bench/fuse_quant.py:234); its arithmetic is the
+ * reference's torch `quant` (tests/test_fused_quant.py:26-31).
+ */
+int i8l_quant_rows(const void *x, int64_t ldx, int32_t act_dtype, int8_t *q,
+                   int64_t ldq, float *scale, int32_t M, int32_t K,
+                   int32_t precise_div, void *stream);
+
+/* One-line message for the last non-OK return on this host thread. */
+const char *i8l_last_error(void);
+
+/*
+ * Device status word, written by kernels whose bounded waits gave up (a wait that
+ * should take microseconds ran past its limit).  i8l_read_status() synchronises
+ * the device and returns the word (0 = clean); i8l_clear_status() resets it.
+ * No reference counterpart (Triton kernels have no in-kernel waits).
+ */
+int i8l_read_status(int32_t *status_out);
+int i8l_clear_status(void);
+
+/* Library version string and the compiled target, e.g. "0.1.0 sm_100a". */
+const char *i8l_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INT8_LINEAR_B200_H */

@@ -1,0 +1,97 @@
+"""Loads libint8linear_b200.so and binds its C ABI (include/int8_linear_b200.h).
+
+There is no fallback: if the library is missing, importing the kernels raises with
+the command that builds it.  Error codes become NotSupported, ValueError or
+RuntimeError, exactly as the reference's launchers raise them.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libint8linear_b200.so"
+
+OK, ENOTSUP, EINVAL, ECUDA, EWORKSPACE = 0, 1, 2, 3, 4
+BF16, F16, F32, I32 = 0, 1, 2, 3
+
+
+class NotSupported(Exception):
+    """The kernel does not take this shape or dtype, so the caller should fall back."""
+
+
+class I8LTile(ctypes.Structure):
+    """Mirror of struct i8l_tile."""
+
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "swap_ab", "tok_tile", "w_tile", "stages", "ctas", "group", "split", "reserved")]
+
+
+_lib = None
+_lock = threading.Lock()
+
+_vp, _i8p, _fp = ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p
+_i32, _i64, _f32, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+
+# name -> (restype, argtypes); the same list the CPU tests check against the header.
+SIGNATURES = {
+    "i8l_w8a8_mm": (_i32, [_i8p, _i64, _i8p, _i64, _fp, _i32, _fp, _i32, _vp, _i32, _vp, _i32, _i64,
+                           _i32, _i32, _i32, ctypes.POINTER(I8LTile), _vp, _sz, _vp]),
+    "i8l_workspace_size": (_sz, [_i32, _i32, _i32, ctypes.POINTER(I8LTile)]),
+    "i8l_default_tile": (_i32, [_i32, _i32, _i32, ctypes.POINTER(I8LTile)]),
+    "i8l_add_rmsnorm_quant": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i32, _i8p, _i64, _fp, _vp, _i64,
+                                     _i32, _i32, _f32, _i32, _vp]),
+    "i8l_silu_mul_quant": (_i32, [_vp, _i64, _i32, _i8p, _i64, _fp, _i32, _i32, _i32, _i32, _vp]),
+    "i8l_quant_rows": (_i32, [_vp, _i64, _i32, _i8p, _i64, _fp, _i32, _i32, _i32, _vp]),
+    "i8l_last_error": (ctypes.c_char_p, []),
+    "i8l_read_status": (_i32, [ctypes.POINTER(_i32)]),
+    "i8l_clear_status": (_i32, []),
+    "i8l_version": (ctypes.c_char_p, []),
+}
+
+
+def load(path: Path | str | None = None) -> ctypes.CDLL:
+    """The bound library (loaded once).  Raises ImportError if it was never built."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            raise ImportError(
+                f"{p} is missing: build the sm_100a library first with "
+                "`python -m int8_linear.build` (there is no non-CUDA fallback)")
+        lib = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(code: int) -> None:
+    """Raise the exception the reference's launcher would raise for this code."""
+    if code == OK:
+        return
+    msg = load().i8l_last_error().decode(errors="replace")
+    if code == ENOTSUP:
+        raise NotSupported(msg)
+    if code == EINVAL:
+        raise ValueError(msg)
+    raise RuntimeError(f"int8_linear native call failed ({code}): {msg}")
+
+
+def read_status() -> int:
+    """Synchronise the device and return the kernels' status word (0 = clean)."""
+    v = _i32(0)
+    check(load().i8l_read_status(ctypes.byref(v)))
+    return int(v.value)
+
+
+def clear_status() -> None:
+    check(load().i8l_clear_status())

@@ -1,0 +1,790 @@
+// W8A8 GEMM for sm_100a: int8 x int8 -> int32 on the tcgen05 tensor cores with
+// the accumulator in TMEM, operands streamed by TMA through a shared-memory
+// ring, and the dequantisation (x scale_a x scale_b + bias, rounded once to the
+// output type) fused into the epilogue.
+//
+// Computes what the reference's Triton kernel _w8a8_mm computes
+// (int8_linear/kernel.py:63-124 in AshrithaG/int8-linear):
+//     out[m,n] = cast( ((float(acc[m,n]) * sa[m]) * sb[n]) + float(bias[n]) )
+// with acc the exact int32 product, or acc itself when the output is int32.
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0  TMA producer  - one thread fills the stage ring (X tile 128x128 B,
+//                           Y tile TNx128 B per stage, 128-byte swizzle);
+//   warp 1  MMA issuer    - one thread issues tcgen05.mma.kind::i8 (M=128, N=TN,
+//                           K=32) into one of two TMEM accumulators;
+//   warps 2-5 epilogue    - tcgen05.ld the accumulator, dequantise and store, or
+//                           add a partial sum into the int32 workspace.
+// X is the operand on the 128-row MMA side, Y the TN-row side.  For decode
+// shapes the weight is X (swap_ab: each tile is 128 output columns by TN
+// tokens); for prefill shapes the activation is X.
+//
+// Work split: the (tile, k-block) iteration space is divided among the CTAs.
+// Whole tiles go round-robin first; the tail (the last partial wave plus one
+// full wave) is divided into equal contiguous k-block ranges (stream-K), so
+// some tiles are computed in pieces by several CTAs.  Each piece adds its int32
+// partial sums into a workspace slot with red.add and counts its k-blocks on the
+// slot's counter; the CTA whose count completes the tile reads the slot, runs
+// the epilogue and zeroes the slot again.  Integer addition is exact and
+// order-free, so the result does not depend on which CTA finishes last, and no
+// CTA ever waits on another.
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace i8l {
+
+constexpr int kBK = 128;        // K bytes per stage: one 128-byte swizzle row
+constexpr int kXRows = 128;     // MMA M
+constexpr int kThreads = 192;   // 6 warps
+constexpr int kEpiWarps = 4;
+constexpr int kXBytes = kXRows * kBK;  // 16 KB
+
+struct GemmArgs {
+  int M, N, K;
+  int tiles_x, tiles_y, kblocks;
+  int total_tiles, dp_tiles;
+  long long sk_iters;
+  int group;
+  int stages;
+  int swap;
+  const float *sa;
+  const float *sb;
+  int sa_per_row, sb_per_col;
+  const void *bias;
+  int bias_dtype;
+  void *out;
+  int out_dtype;
+  long long ldc;
+  int vec_store;
+  int *ws;        // workspace slots, 128*TN int32 each
+  int *counters;  // one k-block counter per slot
+  int *status;
+};
+
+struct Segment {
+  int tile;
+  int kb0, kb1;
+};
+
+// The deterministic sequence of (tile, k-range) segments one CTA processes.
+// Producer, MMA issuer and epilogue each walk their own copy.
+struct Schedule {
+  int dp_next;
+  long long it, it_end;
+
+  __device__ __forceinline__ void init(const GemmArgs &a) {
+    dp_next = blockIdx.x;
+    const long long g = gridDim.x;
+    it = a.sk_iters * static_cast<long long>(blockIdx.x) / g;
+    it_end = a.sk_iters * static_cast<long long>(blockIdx.x + 1) / g;
+  }
+
+  __device__ __forceinline__ bool next(const GemmArgs &a, Segment &s) {
+    if (dp_next < a.dp_tiles) {
+      s.tile = dp_next;
+      s.kb0 = 0;
+      s.kb1 = a.kblocks;
+      dp_next += gridDim.x;
+      return true;
+    }
+    if (it < it_end) {
+      const long long t = it / a.kblocks;
+      const int kb0 = static_cast<int>(it - t * a.kblocks);
+      const long long left = it_end - it;
+      const int kb1 = static_cast<int>(
+          left < static_cast<long long>(a.kblocks - kb0) ? kb0 + left : a.kblocks);
+      s.tile = a.dp_tiles + static_cast<int>(t);
+      s.kb0 = kb0;
+      s.kb1 = kb1;
+      it += kb1 - kb0;
+      return true;
+    }
+    return false;
+  }
+};
+
+// Workspace slot of a stream-K tile that is split: one less than the first CTA
+// whose range starts strictly inside the tile.  Distinct split tiles get
+// distinct slots in [0, gridDim.x - 1).
+__device__ __forceinline__ int split_slot(const GemmArgs &a, int tile) {
+  const long long s = tile - a.dp_tiles;
+  const long long g = gridDim.x;
+  const long long num = (s * a.kblocks + 1) * g;
+  const long long b = (num + a.sk_iters - 1) / a.sk_iters;
+  return static_cast<int>(b - 1);
+}
+
+// Tile index -> (x tile, y tile), walking `group` x tiles together so CTAs that
+// run at the same time share Y tiles in L2.
+__device__ __forceinline__ void tile_coords(const GemmArgs &a, int t, int &tx,
+                                            int &ty) {
+  const int per_group = a.group * a.tiles_y;
+  const int g = t / per_group;
+  const int first = g * a.group;
+  const int gsz = min(a.tiles_x - first, a.group);
+  const int r = t - g * per_group;
+  tx = first + r % gsz;
+  ty = r / gsz;
+}
+
+__device__ __forceinline__ float load_scalar_f(const void *p, int dtype, long long i) {
+  switch (dtype) {
+    case I8L_BF16:
+      return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+    case I8L_F16:
+      return __half2float(static_cast<const __half *>(p)[i]);
+    default:
+      return static_cast<const float *>(p)[i];
+  }
+}
+
+// The reference's epilogue order: float(acc) * sa, then * sb, then + bias, each
+// rounded in fp32 (no contraction into an FMA), then one rounding to the output.
+__device__ __forceinline__ float dequant(int acc, float sa, float sb, float bias,
+                                         bool has_bias) {
+  float v = __int2float_rn(acc);
+  v = __fmul_rn(v, sa);
+  v = __fmul_rn(v, sb);
+  if (has_bias) v = __fadd_rn(v, bias);
+  return v;
+}
+
+__device__ __forceinline__ void store_elem(void *out, int dtype, long long idx,
+                                           int acc, float v) {
+  switch (dtype) {
+    case I8L_BF16:
+      static_cast<__nv_bfloat16 *>(out)[idx] = __float2bfloat16_rn(v);
+      break;
+    case I8L_F16:
+      static_cast<__half *>(out)[idx] = __float2half_rn(v);
+      break;
+    case I8L_F32:
+      static_cast<float *>(out)[idx] = v;
+      break;
+    default:
+      static_cast<int *>(out)[idx] = acc;
+      break;
+  }
+}
+
+// Stores 16 accumulator values of one TMEM lane (`row` of the X tile) for the
+// accumulator columns c0..c0+15 (columns of the Y tile).
+template <int TN>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs &a, int tx, int ty,
+                                               int row, int c0,
+                                               const uint32_t (&r)[16]) {
+  const bool raw = a.out_dtype == I8L_I32;
+  const bool has_bias = a.bias != nullptr;
+  if (a.swap) {
+    // X rows are output columns n, Y rows are tokens m.
+    const int n = tx * kXRows + row;
+    if (n >= a.N) return;
+    const float sb = raw ? 0.f : (a.sb_per_col ? a.sb[n] : a.sb[0]);
+    const float bias = (!raw && has_bias) ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f;
+    const int m0 = ty * TN + c0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = m0 + j;
+      if (m < a.M) {
+        const int acc = static_cast<int>(r[j]);
+        float v = 0.f;
+        if (!raw) v = dequant(acc, a.sa_per_row ? a.sa[m] : a.sa[0], sb, bias, has_bias);
+        store_elem(a.out, a.out_dtype, static_cast<long long>(m) * a.ldc + n, acc, v);
+      }
+    }
+  } else {
+    // X rows are tokens m, Y rows are output columns n.
+    const int m = tx * kXRows + row;
+    if (m >= a.M) return;
+    const int n0 = ty * TN + c0;
+    const long long base = static_cast<long long>(m) * a.ldc + n0;
+    if (raw) {
+      if (a.vec_store && n0 + 16 <= a.N) {
+        int4 *dst = reinterpret_cast<int4 *>(static_cast<int *>(a.out) + base);
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4)
+          dst[v4] = make_int4(r[4 * v4], r[4 * v4 + 1], r[4 * v4 + 2], r[4 * v4 + 3]);
+      } else {
+        for (int j = 0; j < 16 && n0 + j < a.N; ++j)
+          static_cast<int *>(a.out)[base + j] = static_cast<int>(r[j]);
+      }
+      return;
+    }
+    const float sa = a.sa_per_row ? a.sa[m] : a.sa[0];
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = min(n0 + j, a.N - 1);
+      const float sb = a.sb_per_col ? a.sb[n] : a.sb[0];
+      const float bias = has_bias ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f;
+      v[j] = dequant(static_cast<int>(r[j]), sa, sb, bias, has_bias);
+    }
+    if (a.vec_store && n0 + 16 <= a.N) {
+      if (a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16) {
+        uint32_t p[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (a.out_dtype == I8L_BF16) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+            p[j] = *reinterpret_cast<uint32_t *>(&h);
+          } else {
+            __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            p[j] = *reinterpret_cast<uint32_t *>(&h);
+          }
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.out) + base);
+        dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+        dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+      } else {
+        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(a.out) + base);
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4)
+          dst[v4] = make_float4(v[4 * v4], v[4 * v4 + 1], v[4 * v4 + 2], v[4 * v4 + 3]);
+      }
+    } else {
+      for (int j = 0; j < 16 && n0 + j < a.N; ++j)
+        store_elem(a.out, a.out_dtype, base + j, static_cast<int>(r[j]), v[j]);
+    }
+  }
+}
+
+// Number of accumulator columns of a tile that hold real (in-range) Y rows.
+template <int TN>
+__device__ __forceinline__ int live_cols(const GemmArgs &a, int ty) {
+  const int rows_y = a.swap ? a.M : a.N;
+  return min(TN, rows_y - ty * TN);
+}
+
+__device__ __forceinline__ void red_add_s32(int *p, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_cg_s32(const int *p) {
+  int v;
+  asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_cg_s32(int *p, int v) {
+  asm volatile("st.global.cg.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int TN>
+struct SmemLayout {
+  static constexpr int kYBytes = TN * kBK;
+  static constexpr int kStageBytes = kXBytes + kYBytes;
+  static constexpr int kTmemCols = (2 * TN < 32) ? 32 : 2 * TN;
+  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain, + tmem slot, flags
+  static size_t bytes(int stages) {
+    return 1024 /* alignment slack */ + static_cast<size_t>(stages) * kStageBytes +
+           static_cast<size_t>(2 * stages + 5) * 8 + 64;
+  }
+};
+
+template <int TN>
+__global__ void __launch_bounds__(kThreads, 1)
+    w8a8_gemm_sm100(const __grid_constant__ CUtensorMap map_x,
+                    const __grid_constant__ CUtensorMap map_y, const GemmArgs a) {
+  using L = SmemLayout<TN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int S = a.stages;
+  uint8_t *sx = smem;
+  uint8_t *sy = smem + static_cast<size_t>(S) * kXBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(S) * L::kStageBytes);
+  uint64_t *empty = full + S;
+  uint64_t *acc_full = empty + S;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *drain = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *last_flag = abort_flag + 1;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_y);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_x = a.swap ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_y = a.swap ? policy_evict_last() : policy_evict_last();
+      Schedule sch;
+      sch.init(a);
+      Segment seg;
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      while (ok && sch.next(a, seg)) {
+        int tx, ty;
+        tile_coords(a, seg.tile, tx, ty);
+        for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, a.status,
+                                 kStatusProducerWait)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          tma_load_2d(sx + static_cast<size_t>(stage) * kXBytes, &map_x, &full[stage],
+                      kb * kBK, tx * kXRows, pol_x);
+          tma_load_2d(sy + static_cast<size_t>(stage) * L::kYBytes, &map_y, &full[stage],
+                      kb * kBK, ty * TN, pol_y);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the loads already issued land before the CTA exits.
+        int st = stage;
+        uint32_t ph = phase;
+        const long long n = issued < S ? issued : S;
+        for (long long i = 0; i < n; ++i) {
+          if (--st < 0) {
+            st = S - 1;
+            ph ^= 1u;
+          }
+          volatile int no_abort = 0;
+          mbar_wait_bounded(&full[st], ph, &no_abort, a.status, kStatusDrainWait);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_i8(kXRows, TN);
+      Schedule sch;
+      sch.init(a);
+      Segment seg;
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      while (ok && sch.next(a, seg)) {
+        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, abort_flag, a.status,
+                               kStatusMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * TN);
+        for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, a.status,
+                                 kStatusMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_kmajor_desc(smem_u32(sx + static_cast<size_t>(stage) * kXBytes));
+          const uint64_t bd = sw128_kmajor_desc(smem_u32(sy + static_cast<size_t>(stage) * L::kYBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            mma_i8(d, ad + 2 * k, bd + 2 * k, kIdesc, (kb > seg.kb0 || k > 0) ? 1u : 0u);
+          issued_any = true;
+          mma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        // Let the MMAs in flight finish before TMEM and shared memory go away.
+        mma_commit(drain);
+        volatile int no_abort = 0;
+        mbar_wait_bounded(drain, 0, &no_abort, a.status, kStatusDrainWait);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row = quarter * 32 + lane;
+    const int epi_tid = threadIdx.x - 64;
+    Schedule sch;
+    sch.init(a);
+    Segment seg;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    while (sch.next(a, seg)) {
+      const bool ok = mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, a.status,
+                                        kStatusEpilogueWait);
+      // All four epilogue warps continue or all stop: they meet at named barriers below.
+      if (!named_bar_and(2, kEpiWarps * 32, ok)) break;
+      tc_fence_after();
+      int tx, ty;
+      tile_coords(a, seg.tile, tx, ty);
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * TN);
+      const int ncols = live_cols<TN>(a, ty);
+      const bool whole = seg.kb0 == 0 && seg.kb1 == a.kblocks;
+      if (whole) {
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c0, r);
+          tmem_ld_wait();
+          epilogue_chunk<TN>(a, tx, ty, row, c0, r);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      } else {
+        const int slot = split_slot(a, seg.tile);
+        int *ws = a.ws + static_cast<size_t>(slot) * (kXRows * TN);
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) red_add_s32(ws + (c0 + j) * kXRows + row, static_cast<int>(r[j]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        __threadfence();
+        named_bar_sync(1, kEpiWarps * 32);
+        if (epi_tid == 0) {
+          const int mine = seg.kb1 - seg.kb0;
+          const int before = atomicAdd(a.counters + slot, mine);
+          *last_flag = (before + mine == a.kblocks) ? 1 : 0;
+        }
+        named_bar_sync(1, kEpiWarps * 32);
+        if (*last_flag) {
+          __threadfence();
+          for (int c0 = 0; c0 < ncols; c0 += 16) {
+            uint32_t r[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              int *p = ws + (c0 + j) * kXRows + row;
+              r[j] = static_cast<uint32_t>(ld_cg_s32(p));
+              st_cg_s32(p, 0);
+            }
+            epilogue_chunk<TN>(a, tx, ty, row, c0, r);
+          }
+          if (epi_tid == 0) atomicExch(a.counters + slot, 0);
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Tensor map over an int8 [rows, K] matrix with row stride `ld` bytes, boxes of
+// 128 bytes along K by `box_rows` rows, 128-byte swizzle, zero fill outside.
+static int make_operand_map(CUtensorMap *map, const int8_t *ptr, int64_t rows, int64_t k,
+                            int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(I8L_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(I8L_ECUDA, "cuTensorMapEncodeTiled failed (CUresult %d) for [%lld x %lld], ld %lld",
+                     static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(k),
+                     static_cast<long long>(ld));
+  return I8L_OK;
+}
+
+static int max_stages_for(int tn, int smem_optin) {
+  const int stage = kXBytes + tn * kBK;
+  const int avail = smem_optin - 1024 - 256;
+  return std::max(1, std::min(16, avail / stage));
+}
+
+static bool valid_tok_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128 || t == 256; }
+
+// Everything the launch needs, derived from the problem and the tile.
+struct Plan {
+  i8l_tile tile;
+  int tn;  // Y tile rows (MMA N)
+  int tiles_x, tiles_y, kblocks, total_tiles, dp_tiles, ctas;
+  long long sk_iters;
+  int slots;
+  size_t ws_bytes;
+};
+
+static void default_tile(int M, int N, int K, i8l_tile *t) {
+  (void)N;
+  (void)K;
+  *t = i8l_tile{};
+  if (M <= 256) {
+    t->swap_ab = 1;
+    t->tok_tile = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    t->w_tile = 128;
+  } else {
+    t->swap_ab = 0;
+    t->tok_tile = 128;
+    t->w_tile = 256;
+  }
+  t->group = 8;
+}
+
+static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
+  DeviceInfo di;
+  int e = device_info(&di);
+  if (e) return e;
+  i8l_tile t;
+  const bool auto_tile = user == nullptr || (user->tok_tile == 0 && user->w_tile == 0);
+  if (auto_tile) {
+    default_tile(M, N, K, &t);
+    if (user) {
+      if (user->stages) t.stages = user->stages;
+      if (user->ctas) t.ctas = user->ctas;
+      if (user->group) t.group = user->group;
+      t.split = user->split;
+    }
+  } else {
+    t = *user;
+  }
+  if (t.swap_ab) {
+    if (!valid_tok_tile(t.tok_tile) || t.w_tile != 128)
+      return set_error(I8L_ENOTSUP,
+                       "swap_ab tile needs tok_tile in {16,32,64,128,256} and w_tile 128, got %dx%d",
+                       t.tok_tile, t.w_tile);
+    p->tn = t.tok_tile;
+  } else {
+    if (t.tok_tile != 128 || (t.w_tile != 128 && t.w_tile != 256))
+      return set_error(I8L_ENOTSUP, "tile needs tok_tile 128 and w_tile in {128,256}, got %dx%d",
+                       t.tok_tile, t.w_tile);
+    p->tn = t.w_tile;
+  }
+  const int max_st = max_stages_for(p->tn, di.max_smem_optin);
+  if (t.stages <= 0) t.stages = max_st;
+  if (t.stages < 2 || t.stages > max_st)
+    return set_error(I8L_ENOTSUP, "stages %d outside [2, %d] for this tile", t.stages, max_st);
+  if (t.group <= 0) t.group = 1;
+  const int rows_x = t.swap_ab ? N : M;
+  const int rows_y = t.swap_ab ? M : N;
+  p->tiles_x = (rows_x + kXRows - 1) / kXRows;
+  p->tiles_y = (rows_y + p->tn - 1) / p->tn;
+  p->kblocks = (K + kBK - 1) / kBK;
+  p->total_tiles = p->tiles_x * p->tiles_y;
+  const long long total_iters = static_cast<long long>(p->total_tiles) * p->kblocks;
+  int ctas = t.ctas > 0 ? t.ctas : di.sms;
+  if (t.split == 1) {
+    ctas = std::min(ctas, p->total_tiles);
+    p->dp_tiles = p->total_tiles;
+  } else {
+    if (static_cast<long long>(ctas) > total_iters) ctas = static_cast<int>(total_iters);
+    const int waves = p->total_tiles / ctas;
+    if (p->total_tiles % ctas == 0)
+      p->dp_tiles = p->total_tiles;
+    else
+      p->dp_tiles = waves >= 1 ? (waves - 1) * ctas : 0;
+  }
+  t.ctas = ctas;
+  p->ctas = ctas;
+  p->sk_iters = static_cast<long long>(p->total_tiles - p->dp_tiles) * p->kblocks;
+  p->slots = p->sk_iters > 0 ? std::max(1, ctas - 1) : 0;
+  const size_t counters_bytes = ((static_cast<size_t>(p->slots) * 4 + 255) / 256) * 256;
+  p->ws_bytes = p->slots ? counters_bytes + static_cast<size_t>(p->slots) * kXRows * p->tn * 4 : 0;
+  p->tile = t;
+  return I8L_OK;
+}
+
+template <int TN>
+static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const GemmArgs &a, int ctas,
+                     int stages, cudaStream_t stream) {
+  const size_t smem = SmemLayout<TN>::bytes(stages);
+  // Largest dynamic shared memory already allowed, per device (the attribute is
+  // set on the function as loaded in each device's context).
+  static size_t configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64 || smem > configured[dev]) {
+    e = cudaFuncSetAttribute(w8a8_gemm_sm100<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
+    if (dev >= 0 && dev < 64) configured[dev] = smem;
+  }
+  w8a8_gemm_sm100<TN><<<ctas, kThreads, smem, stream>>>(mx, my, a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "gemm launch");
+  return I8L_OK;
+}
+
+}  // namespace i8l
+
+using namespace i8l;
+
+extern "C" int i8l_default_tile(int32_t M, int32_t N, int32_t K, i8l_tile *tile_out) {
+  if (!tile_out) return set_error(I8L_EINVAL, "tile_out is NULL");
+  Plan p;
+  int e = make_plan(M > 0 ? M : 1, N > 0 ? N : 1, K > 0 ? K : 16, nullptr, &p);
+  if (e) return e;
+  *tile_out = p.tile;
+  return I8L_OK;
+}
+
+extern "C" size_t i8l_workspace_size(int32_t M, int32_t N, int32_t K, const i8l_tile *tile) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  Plan p;
+  if (make_plan(M, N, K, tile, &p)) return 0;
+  return p.ws_bytes;
+}
+
+extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
+                           const float *sa, int32_t sa_per_row, const float *sb,
+                           int32_t sb_per_col, const void *bias, int32_t bias_dtype, void *out,
+                           int32_t out_dtype, int64_t ldc, int32_t M, int32_t N, int32_t K,
+                           const i8l_tile *tile, void *workspace, size_t ws_bytes, void *stream) {
+  if (M < 0 || N < 0 || K < 0) return set_error(I8L_EINVAL, "negative size M=%d N=%d K=%d", M, N, K);
+  if (out_dtype < I8L_BF16 || out_dtype > I8L_I32)
+    return set_error(I8L_ENOTSUP, "output dtype code %d not supported", out_dtype);
+  if (M == 0 || N == 0) return I8L_OK;
+  if (K == 0) return set_error(I8L_ENOTSUP, "K=0 is not supported");
+  if (!A || !W || !out) return set_error(I8L_EINVAL, "NULL operand pointer");
+  if (K % 16) return set_error(I8L_ENOTSUP, "K=%d must be a multiple of 16", K);
+  if (lda < K || ldw < K || ldc < N)
+    return set_error(I8L_EINVAL, "leading dimensions lda=%lld ldw=%lld ldc=%lld too small",
+                     static_cast<long long>(lda), static_cast<long long>(ldw),
+                     static_cast<long long>(ldc));
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W)) % 16 || lda % 16 || ldw % 16)
+    return set_error(I8L_ENOTSUP, "int8 operands and their row strides must be 16-byte aligned");
+  const bool raw = out_dtype == I8L_I32;
+  if (!raw) {
+    if (!sa || !sb) return set_error(I8L_EINVAL, "NULL scale pointer");
+    if (bias && (bias_dtype < I8L_BF16 || bias_dtype > I8L_F32))
+      return set_error(I8L_ENOTSUP, "bias dtype code %d not supported", bias_dtype);
+  }
+  Plan p;
+  int e = make_plan(M, N, K, tile, &p);
+  if (e) return e;
+  if (p.ws_bytes > 0 && (workspace == nullptr || ws_bytes < p.ws_bytes))
+    return set_error(I8L_EWORKSPACE, "workspace of %zu bytes needed, %zu given", p.ws_bytes,
+                     workspace ? ws_bytes : static_cast<size_t>(0));
+  if (workspace && reinterpret_cast<uintptr_t>(workspace) % 256)
+    return set_error(I8L_EINVAL, "workspace must be 256-byte aligned");
+
+  CUtensorMap mx, my;
+  const bool swap = p.tile.swap_ab != 0;
+  const int8_t *xp = swap ? W : A;
+  const int8_t *yp = swap ? A : W;
+  const int64_t xrows = swap ? N : M, yrows = swap ? M : N;
+  const int64_t xld = swap ? ldw : lda, yld = swap ? lda : ldw;
+  if ((e = make_operand_map(&mx, xp, xrows, K, xld, kXRows))) return e;
+  if ((e = make_operand_map(&my, yp, yrows, K, yld, p.tn))) return e;
+
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.tiles_x = p.tiles_x;
+  a.tiles_y = p.tiles_y;
+  a.kblocks = p.kblocks;
+  a.total_tiles = p.total_tiles;
+  a.dp_tiles = p.dp_tiles;
+  a.sk_iters = p.sk_iters;
+  a.group = std::max(1, std::min(p.tile.group, p.tiles_x));
+  a.stages = p.tile.stages;
+  a.swap = swap ? 1 : 0;
+  a.sa = sa;
+  a.sb = sb;
+  a.sa_per_row = sa_per_row ? 1 : 0;
+  a.sb_per_col = sb_per_col ? 1 : 0;
+  a.bias = raw ? nullptr : bias;
+  a.bias_dtype = bias_dtype;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.ldc = ldc;
+  const int esize = (out_dtype == I8L_BF16 || out_dtype == I8L_F16) ? 2 : 4;
+  a.vec_store = (reinterpret_cast<uintptr_t>(out) % 16 == 0 && (ldc * esize) % 16 == 0) ? 1 : 0;
+  if (p.ws_bytes) {
+    const size_t counters_bytes = ((static_cast<size_t>(p.slots) * 4 + 255) / 256) * 256;
+    a.counters = static_cast<int *>(workspace);
+    a.ws = reinterpret_cast<int *>(static_cast<uint8_t *>(workspace) + counters_bytes);
+  }
+  a.status = status_ptr();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (p.tn) {
+    case 16:
+      return launch_tn<16>(mx, my, a, p.ctas, a.stages, s);
+    case 32:
+      return launch_tn<32>(mx, my, a, p.ctas, a.stages, s);
+    case 64:
+      return launch_tn<64>(mx, my, a, p.ctas, a.stages, s);
+    case 128:
+      return launch_tn<128>(mx, my, a, p.ctas, a.stages, s);
+    case 256:
+      return launch_tn<256>(mx, my, a, p.ctas, a.stages, s);
+    default:
+      return set_error(I8L_ENOTSUP, "no kernel for tile width %d", p.tn);
+  }
+}

@@ -1,0 +1,445 @@
+// Per-token int8 quantisers fused into the op before them, for sm_100a:
+//   add + RMSNorm + quantise   (reference: int8_linear/fused_quant.py:56-73)
+//   SiLU-and-mul + quantise    (reference: int8_linear/fused_quant.py:76-88)
+//   plain per-token quantise   (the step the reference leaves to vLLM's
+//                               scaled_int8_quant; arithmetic of the reference's
+//                               torch `quant`, tests/test_fused_quant.py:26-31)
+// One CTA per token row.  Each thread holds its slice of the row in registers
+// (16-byte vector loads when the row allows, else scalar loads), so the row is
+// read from HBM once; the sum of squares and the absolute maximum are reduced with
+// warp shuffles and one shared-memory exchange.
+//
+// Arithmetic follows the reference kernels step by step (fused_quant.py:41-88):
+// fp32 math, rounding through the activation/weight dtypes where the reference
+// rounds, CUDA's rsqrtf/expf where the reference calls libdevice rsqrt/exp,
+// Triton's approximate `/` (div.full.f32) where the reference uses a plain
+// divide, IEEE division for the quantiser when precise_div is set, and
+// round-half-to-even with saturation to [-128, 127].
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace i8l {
+
+// Both reductions leave the result in every thread.  `red` holds 32 floats.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < nw ? red[l] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < nw ? red[l] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Which row elements thread t owns: vector v (0..NV-1) covers columns
+// [(v*blockDim + t)*VW, +VW).  VW is 8 (16-byte vectors of 16-bit values) or 1.
+template <int VW>
+__device__ __forceinline__ int col_of(int v) {
+  return (v * blockDim.x + threadIdx.x) * VW;
+}
+
+template <int DT, int VW>
+__device__ __forceinline__ void load_vec(const void *row, int col, float (&out)[VW]) {
+  using T = typename ActType<DT>::T;
+  const T *p = static_cast<const T *>(row) + col;
+  if constexpr (VW == 8 && sizeof(T) == 2) {
+    const uint4 raw = *reinterpret_cast<const uint4 *>(p);
+    const T *h = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = ActType<DT>::to_f32(h[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VW; ++i) out[i] = ActType<DT>::to_f32(p[i]);
+  }
+}
+
+template <int DT, int VW>
+__device__ __forceinline__ void store_vec(void *row, int col, const float (&in)[VW]) {
+  using T = typename ActType<DT>::T;
+  T *p = static_cast<T *>(row) + col;
+  if constexpr (VW == 8 && sizeof(T) == 2) {
+    uint4 raw;
+    T *h = reinterpret_cast<T *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = ActType<DT>::from_f32(in[i]);
+    *reinterpret_cast<uint4 *>(p) = raw;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VW; ++i) p[i] = ActType<DT>::from_f32(in[i]);
+  }
+}
+
+__device__ __forceinline__ float load_weight(const void *w, int dtype, int col) {
+  switch (dtype) {
+    case I8L_BF16:
+      return __bfloat162float(static_cast<const __nv_bfloat16 *>(w)[col]);
+    case I8L_F16:
+      return __half2float(static_cast<const __half *>(w)[col]);
+    default:
+      return static_cast<const float *>(w)[col];
+  }
+}
+
+// Rounds an fp32 value to the weight dtype and back (the reference's
+// xn.to(w.dtype)); fp32 weights leave it unchanged.
+__device__ __forceinline__ float round_to_weight(float v, int dtype) {
+  switch (dtype) {
+    case I8L_BF16:
+      return round_through<I8L_BF16>(v);
+    case I8L_F16:
+      return round_through<I8L_F16>(v);
+    default:
+      return v;
+  }
+}
+
+// The row quantiser of the reference (_quantize_row, fused_quant.py:41-53):
+// scale = absmax/127, inv = 127/absmax (0 for a zero row), q = rint(y*inv)
+// saturated to [-128, 127].  `y` holds this thread's values (0 where the thread
+// owns no column), `valid` marks the real ones.
+template <int NV, int VW>
+__device__ __forceinline__ void quantize_row(const float (&y)[NV][VW], int K, int8_t *qrow,
+                                             float *scale_out, int precise, float *red) {
+  float amax = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int i = 0; i < VW; ++i) amax = fmaxf(amax, fabsf(y[v][i]));
+  amax = block_max(amax, red);
+  const float scale = precise ? div_rn(amax, 127.f) : div_full(amax, 127.f);
+  const float inv = amax == 0.f ? 0.f : (precise ? div_rn(127.f, amax) : div_full(127.f, amax));
+  if (threadIdx.x == 0) *scale_out = scale;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int col = col_of<VW>(v);
+    if (col >= K) continue;
+    int8_t q[VW];
+#pragma unroll
+    for (int i = 0; i < VW; ++i) {
+      int r = __float2int_rn(__fmul_rn(y[v][i], inv));
+      r = r < -128 ? -128 : (r > 127 ? 127 : r);
+      q[i] = static_cast<int8_t>(r);
+    }
+    if constexpr (VW == 8) {
+      *reinterpret_cast<uint2 *>(qrow + col) = *reinterpret_cast<const uint2 *>(q);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) qrow[col + i] = q[i];
+    }
+  }
+}
+
+struct NormArgs {
+  const void *x;
+  long long ldx;
+  const void *res;
+  long long ldr;
+  const void *w;
+  int w_dtype;
+  int8_t *q;
+  long long ldq;
+  float *scale;
+  void *rout;
+  long long ldro;
+  int K;
+  float eps;
+  int precise;
+};
+
+template <int DT, int NV, int VW>
+__global__ void __launch_bounds__(VW == 8 ? 256 : 1024) add_rmsnorm_quant_kernel(const NormArgs a) {
+  __shared__ float red[32];
+  using T = typename ActType<DT>::T;
+  const long long row = blockIdx.x;
+  const T *xrow = static_cast<const T *>(a.x) + row * a.ldx;
+  float x[NV][VW];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int col = col_of<VW>(v);
+    if (col < a.K) {
+      load_vec<DT, VW>(xrow, col, x[v]);
+      if (a.res) {
+        float r[VW];
+        load_vec<DT, VW>(static_cast<const T *>(a.res) + row * a.ldr, col, r);
+#pragma unroll
+        for (int i = 0; i < VW; ++i) x[v][i] = __fadd_rn(x[v][i], r[i]);
+        store_vec<DT, VW>(static_cast<T *>(a.rout) + row * a.ldro, col, x[v]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) x[v][i] = 0.f;
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int i = 0; i < VW; ++i) ss = __fadd_rn(ss, __fmul_rn(x[v][i], x[v][i]));
+  ss = block_sum(ss, red);
+  // var = sum(x^2) / K with Triton's plain `/`, then xn = x * rsqrt(var + eps).
+  const float var = div_full(ss, static_cast<float>(a.K));
+  const float rs = rsqrtf(__fadd_rn(var, a.eps));
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int col = col_of<VW>(v);
+#pragma unroll
+    for (int i = 0; i < VW; ++i) {
+      if (col < a.K) {
+        const float xn = round_to_weight(__fmul_rn(x[v][i], rs), a.w_dtype);
+        const float wv = load_weight(a.w, a.w_dtype, col + i);
+        x[v][i] = round_through<DT>(__fmul_rn(xn, wv));
+      }
+    }
+  }
+  quantize_row<NV, VW>(x, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red);
+}
+
+struct SiluArgs {
+  const void *gu;
+  long long ld;
+  int8_t *q;
+  long long ldq;
+  float *scale;
+  int I;
+  int precise;
+  int round_silu;
+};
+
+template <int DT, int NV, int VW>
+__global__ void __launch_bounds__(VW == 8 ? 256 : 1024) silu_mul_quant_kernel(const SiluArgs a) {
+  __shared__ float red[32];
+  using T = typename ActType<DT>::T;
+  const long long row = blockIdx.x;
+  const T *grow = static_cast<const T *>(a.gu) + row * a.ld;
+  const T *urow = grow + a.I;
+  float y[NV][VW];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int col = col_of<VW>(v);
+    if (col < a.I) {
+      float g[VW], u[VW];
+      load_vec<DT, VW>(grow, col, g);
+      load_vec<DT, VW>(urow, col, u);
+#pragma unroll
+      for (int i = 0; i < VW; ++i) {
+        // silu(g) = g / (1 + exp(-g)) with Triton's plain `/`.
+        float s = div_full(g[i], __fadd_rn(1.0f, expf(-g[i])));
+        if (a.round_silu) s = round_through<DT>(s);
+        y[v][i] = round_through<DT>(__fmul_rn(s, u[i]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) y[v][i] = 0.f;
+    }
+  }
+  quantize_row<NV, VW>(y, a.I, a.q + row * a.ldq, a.scale + row, a.precise, red);
+}
+
+struct QuantArgs {
+  const void *x;
+  long long ldx;
+  int8_t *q;
+  long long ldq;
+  float *scale;
+  int K;
+  int precise;
+};
+
+template <int DT, int NV, int VW>
+__global__ void __launch_bounds__(VW == 8 ? 256 : 1024) quant_rows_kernel(const QuantArgs a) {
+  __shared__ float red[32];
+  using T = typename ActType<DT>::T;
+  const long long row = blockIdx.x;
+  const T *xrow = static_cast<const T *>(a.x) + row * a.ldx;
+  float y[NV][VW];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int col = col_of<VW>(v);
+    if (col < a.K) {
+      load_vec<DT, VW>(xrow, col, y[v]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) y[v][i] = 0.f;
+    }
+  }
+  quantize_row<NV, VW>(y, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red);
+}
+
+// ------------------------------------------------------------------ launch
+
+// Threads and values per thread for a row of `cols` values: vectors of VW
+// values, the fewest vectors per thread that keep the CTA at <= 256 threads
+// (the scalar path may grow to 1024 threads of 16 values).
+struct RowShape {
+  int nv;
+  int threads;
+};
+
+static bool row_shape(int cols, int vw, RowShape *s) {
+  const int vecs = (cols + vw - 1) / vw;
+  static const int kNv[] = {1, 2, 3, 4, 6, 8, 12, 16};
+  for (int nv : kNv) {
+    int threads = (vecs + nv - 1) / nv;
+    threads = ((threads + 31) / 32) * 32;
+    if (threads <= 256 || (vw == 1 && nv == 16 && threads <= 1024)) {
+      s->nv = nv;
+      s->threads = std::max(32, threads);
+      return true;
+    }
+  }
+  return false;
+}
+
+static bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+#define I8L_DISPATCH_NV(NVVAL, ...)                                                \
+  switch (NVVAL) {                                                                 \
+    case 1: { constexpr int NV = 1; __VA_ARGS__; } break;                          \
+    case 2: { constexpr int NV = 2; __VA_ARGS__; } break;                          \
+    case 3: { constexpr int NV = 3; __VA_ARGS__; } break;                          \
+    case 4: { constexpr int NV = 4; __VA_ARGS__; } break;                          \
+    case 6: { constexpr int NV = 6; __VA_ARGS__; } break;                          \
+    case 8: { constexpr int NV = 8; __VA_ARGS__; } break;                          \
+    case 12: { constexpr int NV = 12; __VA_ARGS__; } break;                        \
+    default: { constexpr int NV = 16; __VA_ARGS__; } break;                        \
+  }
+
+}  // namespace i8l
+
+using namespace i8l;
+
+namespace {
+
+int check_act(int act) {
+  if (act != I8L_BF16 && act != I8L_F16)
+    return set_error(I8L_ENOTSUP, "activation dtype code %d not supported (bf16 or fp16)", act);
+  return I8L_OK;
+}
+
+int finish_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, what);
+  return I8L_OK;
+}
+
+}  // namespace
+
+extern "C" int i8l_add_rmsnorm_quant(const void *x, int64_t ldx, const void *residual,
+                                     int64_t ldr, const void *weight, int32_t act_dtype,
+                                     int32_t w_dtype, int8_t *q, int64_t ldq, float *scale,
+                                     void *rout, int64_t ldro, int32_t M, int32_t K, float eps,
+                                     int32_t precise_div, void *stream) {
+  int e = check_act(act_dtype);
+  if (e) return e;
+  if (w_dtype < I8L_BF16 || w_dtype > I8L_F32)
+    return set_error(I8L_ENOTSUP, "weight dtype code %d not supported", w_dtype);
+  if (M < 0 || K <= 0) return set_error(I8L_EINVAL, "bad size M=%d K=%d", M, K);
+  if (M == 0) return I8L_OK;
+  if (!x || !weight || !q || !scale) return set_error(I8L_EINVAL, "NULL pointer argument");
+  if ((residual == nullptr) != (rout == nullptr))
+    return set_error(I8L_EINVAL, "residual and residual_out must be given together");
+  if (ldx < K || ldq < K || (residual && (ldr < K || ldro < K)))
+    return set_error(I8L_EINVAL, "row stride smaller than K");
+  NormArgs a{x, ldx, residual, ldr, weight, w_dtype, q, ldq, scale, rout, ldro, K, eps, precise_div};
+  const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldq % 8 == 0 && aligned16(x) && aligned16(q) &&
+                   (!residual || (ldr % 8 == 0 && ldro % 8 == 0 && aligned16(residual) &&
+                                  aligned16(rout)));
+  RowShape rs;
+  if (!row_shape(K, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nv = rs.nv, th = rs.threads;
+  if (act_dtype == I8L_BF16) {
+    if (vec) {
+      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_BF16, NV, 8><<<M, th, 0, s>>>(a)))
+    } else {
+      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_BF16, NV, 1><<<M, th, 0, s>>>(a)))
+    }
+  } else {
+    if (vec) {
+      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_F16, NV, 8><<<M, th, 0, s>>>(a)))
+    } else {
+      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_F16, NV, 1><<<M, th, 0, s>>>(a)))
+    }
+  }
+  return finish_launch("add_rmsnorm_quant launch");
+}
+
+extern "C" int i8l_silu_mul_quant(const void *gate_up, int64_t ld, int32_t act_dtype, int8_t *q,
+                                  int64_t ldq, float *scale, int32_t M, int32_t I,
+                                  int32_t precise_div, int32_t round_silu, void *stream) {
+  int e = check_act(act_dtype);
+  if (e) return e;
+  if (M < 0 || I <= 0) return set_error(I8L_EINVAL, "bad size M=%d I=%d", M, I);
+  if (M == 0) return I8L_OK;
+  if (!gate_up || !q || !scale) return set_error(I8L_EINVAL, "NULL pointer argument");
+  if (ld < 2LL * I || ldq < I) return set_error(I8L_EINVAL, "row stride too small");
+  SiluArgs a{gate_up, ld, q, ldq, scale, I, precise_div, round_silu};
+  const bool vec = I % 8 == 0 && ld % 8 == 0 && ldq % 8 == 0 && aligned16(gate_up) && aligned16(q);
+  RowShape rs;
+  if (!row_shape(I, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", I);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nv = rs.nv, th = rs.threads;
+  if (act_dtype == I8L_BF16) {
+    if (vec) {
+      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_BF16, NV, 8><<<M, th, 0, s>>>(a)))
+    } else {
+      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_BF16, NV, 1><<<M, th, 0, s>>>(a)))
+    }
+  } else {
+    if (vec) {
+      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_F16, NV, 8><<<M, th, 0, s>>>(a)))
+    } else {
+      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_F16, NV, 1><<<M, th, 0, s>>>(a)))
+    }
+  }
+  return finish_launch("silu_mul_quant launch");
+}
+
+extern "C" int i8l_quant_rows(const void *x, int64_t ldx, int32_t act_dtype, int8_t *q,
+                              int64_t ldq, float *scale, int32_t M, int32_t K,
+                              int32_t precise_div, void *stream) {
+  int e = check_act(act_dtype);
+  if (e) return e;
+  if (M < 0 || K <= 0) return set_error(I8L_EINVAL, "bad size M=%d K=%d", M, K);
+  if (M == 0) return I8L_OK;
+  if (!x || !q || !scale) return set_error(I8L_EINVAL, "NULL pointer argument");
+  if (ldx < K || ldq < K) return set_error(I8L_EINVAL, "row stride smaller than K");
+  QuantArgs a{x, ldx, q, ldq, scale, K, precise_div};
+  const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldq % 8 == 0 && aligned16(x) && aligned16(q);
+  RowShape rs;
+  if (!row_shape(K, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nv = rs.nv, th = rs.threads;
+  if (act_dtype == I8L_BF16) {
+    if (vec) {
+      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_BF16, NV, 8><<<M, th, 0, s>>>(a)))
+    } else {
+      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_BF16, NV, 1><<<M, th, 0, s>>>(a)))
+    }
+  } else {
+    if (vec) {
+      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_F16, NV, 8><<<M, th, 0, s>>>(a)))
+    } else {
+      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_F16, NV, 1><<<M, th, 0, s>>>(a)))
+    }
+  }
+  return finish_launch("quant_rows launch");
+}

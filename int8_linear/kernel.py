@@ -1,0 +1,232 @@
+"""W8A8 int8 matmul with the dequantisation fused in, on B200 (sm_100a).
+
+    C[M, N] = (A_q[M, K] @ W_q[K, N]) * scale_a[M] * scale_b[N] + bias[N]
+
+Same Python API as the reference module int8_linear/kernel.py (AshrithaG/int8-linear):
+w8a8_mm, Config, NotSupported, default_config, tuned_config, choose_config.  The
+work is done by the hand-written sm_100a kernel in csrc/gemm_sm100.cu (tcgen05
+kind::i8 MMA, TMEM accumulators, TMA pipeline, fused epilogue), reached through the
+C ABI of libint8linear_b200.so; there is no Triton and no CPU path.
+
+W_q is the transposed [K, N] view of an [N, K] nn.Linear weight (strides (1, K)),
+which is how vLLM passes it; both operands are then K-contiguous, the layout the
+tensor cores read.  The launch goes straight from Python to the C ABI on torch's
+current stream, so there is no JIT dispatch to cache: `cached_launch` is accepted
+for compatibility and has no effect.  Under torch.compile, call the kernel through
+the custom op in int8_linear/vllm_patch.py rather than tracing into it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+from dataclasses import dataclass
+from functools import lru_cache
+from pathlib import Path
+
+import torch
+
+from int8_linear import _native
+from int8_linear._native import NotSupported
+
+TUNED_PATH = Path(__file__).with_name("tuned_configs.json")
+TOKEN_TILES = (16, 32, 64, 128, 256)
+# Split-K workspace kept per (device, stream); kernels leave it zero-filled.  The
+# largest plan needs (SMs - 1) slots of 128 x 256 int32 plus counters, ~19 MB on
+# 148 SMs, so one allocation covers every call.
+WORKSPACE_BYTES = 32 << 20
+
+__all__ = ["Config", "NotSupported", "default_config", "tuned_config", "choose_config", "w8a8_mm"]
+
+
+@dataclass(frozen=True)
+class Config:
+    """One B200 GEMM tiling.
+
+    bm      token tile.  With swap_ab the tokens are the MMA N side, bm in
+            {16, 32, 64, 128, 256}; without, they fill the 128-row MMA M side, bm = 128.
+    bn      weight tile: 128 with swap_ab (the MMA M side), else 128 or 256.
+    bk      K bytes per pipeline stage; 128 (one 128-byte swizzle row).
+    warps   warps per CTA: one TMA producer, one MMA issuer, four epilogue warps.
+    stages  shared-memory ring depth, 0 for the most that fits.
+    group_m 128-row tiles walked together so concurrent CTAs share tiles in L2.
+    swap_ab None picks swap_ab for bm != 128.
+    split   0: stream-K over the SMs with an exact int32 fix-up; 1: whole tiles only.
+    ctas    persistent CTAs, 0 for one per SM.
+    """
+
+    bm: int
+    bn: int
+    bk: int = 128
+    warps: int = 6
+    stages: int = 0
+    group_m: int = 8
+    swap_ab: bool | None = None
+    split: int = 0
+    ctas: int = 0
+
+    @property
+    def swapped(self) -> bool:
+        return self.bm != 128 if self.swap_ab is None else bool(self.swap_ab)
+
+    @property
+    def name(self) -> str:
+        tail = (" swap" if self.swapped else "") + (" whole" if self.split == 1 else "")
+        tail += f" c{self.ctas}" if self.ctas else ""
+        return f"{self.bm}x{self.bn}x{self.bk} w{self.warps} s{self.stages} g{self.group_m}{tail}"
+
+    def check(self) -> None:
+        """Raise NotSupported unless a B200 kernel exists for this tiling."""
+        if self.bk != 128 or self.warps != 6:
+            raise NotSupported(f"{self.name}: B200 tiles use bk=128 and 6 warps")
+        if self.swapped:
+            if self.bm not in TOKEN_TILES or self.bn != 128:
+                raise NotSupported(f"{self.name}: swap_ab tiles are bm in {TOKEN_TILES} x bn 128")
+        elif self.bm != 128 or self.bn not in (128, 256):
+            raise NotSupported(f"{self.name}: tiles are bm 128 x bn in (128, 256)")
+        if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1):
+            raise NotSupported(f"{self.name}: bad stages/group_m/split")
+
+    def as_tile(self) -> _native.I8LTile:
+        return _native.I8LTile(
+            swap_ab=1 if self.swapped else 0, tok_tile=self.bm if self.swapped else 128,
+            w_tile=128 if self.swapped else self.bn, stages=self.stages, ctas=self.ctas,
+            group=self.group_m, split=self.split, reserved=0)
+
+
+def default_config(m: int, n: int, k: int) -> Config:
+    """The untuned choice.  Decode batches (M <= 256) put the weight on the 128-row
+    MMA side and the tokens on the narrow side, the smallest token tile that holds
+    M; larger batches use 128 x 256 tiles.  Both split K across the SMs (stream-K)
+    whenever whole tiles would leave SMs idle."""
+    if m <= 256:
+        return Config(next(t for t in TOKEN_TILES if t >= m), 128)
+    return Config(128, 256)
+
+
+@lru_cache(maxsize=None)
+def _tuned_table(device_name: str) -> dict:
+    tables = json.loads(TUNED_PATH.read_text()) if TUNED_PATH.exists() else {}
+    return tables.get(device_name, {})
+
+
+def tuned_config(m: int, n: int, k: int) -> Config | None:
+    """The fastest measured config for this GPU and shape, from the largest tuned
+    batch bucket at or below M, or None if nothing has been tuned."""
+    table = _tuned_table(torch.cuda.get_device_name()).get(f"{k}x{n}", {})
+    fits = [int(bucket) for bucket in table if int(bucket) <= m]
+    return Config(**table[str(max(fits))]["config"]) if fits else None
+
+
+_chosen: dict[tuple[int, int, int, int], Config] = {}
+
+
+def choose_config(m: int, n: int, k: int) -> Config:
+    """tuned_config, else default_config, remembered per device and shape."""
+    key = (torch.cuda.current_device(), m, n, k)
+    cfg = _chosen.get(key)
+    if cfg is None:
+        cfg = _chosen[key] = tuned_config(m, n, k) or default_config(m, n, k)
+    return cfg
+
+
+_DTYPE_CODE = {torch.bfloat16: _native.BF16, torch.float16: _native.F16, torch.float32: _native.F32}
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def workspace(device: torch.device, stream: int) -> torch.Tensor:
+    """The zero-filled split-K workspace for this device and stream (allocated once)."""
+    key = (device.index, stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        ws = _workspaces[key] = torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8, device=device)
+    return ws
+
+
+def _aligned_rows(t: torch.Tensor) -> torch.Tensor:
+    """t itself when its rows start on 16-byte boundaries (what TMA needs), else an
+    aligned contiguous copy.  The reference takes any pointer; this keeps odd
+    pointers exact at the cost of one copy."""
+    if t.stride(1) == 1 and t.data_ptr() % 16 == 0 and t.stride(0) % 16 == 0:
+        return t
+    out = torch.empty(t.shape, dtype=t.dtype, device=t.device)
+    out.copy_(t)
+    return out
+
+
+def w8a8_mm(
+    a_q: torch.Tensor,
+    b_q: torch.Tensor,
+    scale_a: torch.Tensor,
+    scale_b: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    bias: torch.Tensor | None = None,
+    *,
+    config: Config | None = None,
+    raw: bool = False,
+    cached_launch: bool = True,
+) -> torch.Tensor:
+    """(A_q @ B_q) * scale_a * scale_b + bias, for int8 A_q [M, K] and B_q [K, N].
+
+    scale_a is per row ([M] or [M, 1]) or a scalar, scale_b per column ([N] or
+    [N, 1]) or a scalar, both float32.  With raw=True the exact int32 product is
+    returned and the scales and bias are ignored.  Raises NotSupported for what the
+    kernel does not take (the caller may fall back) and ValueError for inconsistent
+    arguments, as the reference does (int8_linear/kernel.py:221-240).
+    """
+    del cached_launch  # launches never go through a JIT dispatch here
+    if a_q.dtype != torch.int8 or b_q.dtype != torch.int8:
+        raise NotSupported(f"int8 operands only, got {a_q.dtype} and {b_q.dtype}")
+    if a_q.dim() != 2 or b_q.dim() != 2 or a_q.shape[1] != b_q.shape[0]:
+        raise ValueError(f"cannot multiply {tuple(a_q.shape)} by {tuple(b_q.shape)}")
+    m, k = a_q.shape
+    n = b_q.shape[1]
+    cfg = config or choose_config(m, n, k)
+    cfg.check()
+    if k % 16:
+        raise NotSupported(f"K={k} must be a multiple of 16 (TMA rows of 16-byte granules)")
+    if n > 1 and b_q.stride(0) != 1:
+        raise NotSupported("B_q must be the K-contiguous [K, N] view of an [N, K] weight")
+    sa, sb = scale_a.reshape(-1).contiguous(), scale_b.reshape(-1).contiguous()
+    if sa.dtype != torch.float32 or sb.dtype != torch.float32:
+        raise NotSupported(f"float32 scales only, got {sa.dtype} and {sb.dtype}")
+    if sa.numel() not in (1, m) or sb.numel() not in (1, n):
+        raise ValueError(f"scale sizes {sa.numel()} and {sb.numel()} fit neither {m} nor {n}")
+    if bias is not None and tuple(bias.shape) != (n,):
+        raise ValueError(f"bias must have shape ({n},), got {tuple(bias.shape)}")
+    if bias is not None:
+        if bias.dtype not in _DTYPE_CODE:
+            raise NotSupported(f"bias dtype {bias.dtype} not supported")
+        bias = bias.contiguous()
+    if not raw and out_dtype not in _DTYPE_CODE:
+        raise NotSupported(f"output dtype {out_dtype} not supported")
+    if not (a_q.is_cuda and b_q.is_cuda and sa.is_cuda and sb.is_cuda):
+        raise ValueError("w8a8_mm runs on a CUDA device; got tensors on "
+                         f"{a_q.device}, {b_q.device}, {sa.device}, {sb.device}")
+
+    out = torch.empty((m, n), dtype=torch.int32 if raw else out_dtype, device=a_q.device)
+    if m == 0 or n == 0:
+        return out
+    a = _aligned_rows(a_q)
+    w = _aligned_rows(b_q.t())
+    lib = _native.load()
+    stream = torch.cuda.current_stream(a_q.device).cuda_stream
+    ws = workspace(a_q.device, stream)
+    tile = cfg.as_tile()
+    if a_q.device.index != torch.cuda.current_device():
+        with torch.cuda.device(a_q.device):
+            code = _launch(lib, a, w, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream)
+    else:
+        code = _launch(lib, a, w, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream)
+    _native.check(code)
+    return out
+
+
+def _launch(lib, a, w, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream) -> int:
+    return lib.i8l_w8a8_mm(
+        a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0),
+        sa.data_ptr(), int(sa.numel() > 1), sb.data_ptr(), int(sb.numel() > 1),
+        bias.data_ptr() if bias is not None else None,
+        _DTYPE_CODE[bias.dtype] if bias is not None else 0,
+        out.data_ptr(), _native.I32 if raw else _DTYPE_CODE[out_dtype], out.stride(0),
+        m, n, k, ctypes.byref(tile), ws.data_ptr(), ws.numel(), stream)

@@ -1,0 +1,102 @@
+"""A 28-layer Qwen3-1.7B-shaped decoder with attention left out, on this library's kernels.
+
+The reference measures its fused path on this stand-in (bench/fuse_quant.py:184-240,
+class Stack, method fused): every layer has its own seeded int8 weights, and one decode
+step runs, per layer,
+
+    add_rmsnorm_quant -> qkv GEMM -> (first 2048 columns) per-token quant -> o_proj GEMM
+    -> add_rmsnorm_quant -> gate_up GEMM -> silu_mul_quant -> down GEMM
+
+captured as one CUDA graph.  Here the qkv slice is quantised in place (the quantiser
+reads rows with a stride), where the reference copies it with .contiguous() and then
+calls vLLM's scaled_int8_quant; the values are the same.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from int8_linear.fused_quant import add_rmsnorm_quant, per_token_quant, silu_mul_quant
+from int8_linear.kernel import w8a8_mm
+
+HIDDEN, INTER, EPS, LAYERS = 2048, 6144, 1e-6, 28
+# (K, N) of each linear, as vLLM runs Qwen3-1.7B (merged qkv and gate_up).
+SHAPES = {"qkv_proj": (2048, 4096), "o_proj": (2048, 2048),
+          "gate_up_proj": (2048, 12288), "down_proj": (6144, 2048)}
+
+
+@dataclass
+class Linear:
+    w_t: torch.Tensor    # [K, N] view of the [N, K] int8 weight (K-contiguous)
+    scale: torch.Tensor  # [N, 1] float32
+
+
+def make_layers(layers: int = LAYERS, seed: int = 0, device="cuda", shapes=SHAPES,
+                generator: torch.Generator | None = None) -> list[dict[str, Linear]]:
+    """Per-layer int8 weights randint(-127, 128) and scales rand*1e-3 + 1e-4, drawn from one
+    seeded generator in layer order (bench/fuse_quant.py:194-199)."""
+    g = generator or torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for _ in range(layers):
+        layer = {}
+        for name, (k, n) in shapes.items():
+            wq = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
+            layer[name] = Linear(wq.t(), torch.rand((n, 1), generator=g, device=device) * 1e-3 + 1e-4)
+        out.append(layer)
+    return out
+
+
+class StandinDecoder:
+    """The reference's fused stand-in step for a decode batch of m tokens."""
+
+    def __init__(self, m: int, layers: int = LAYERS, seed: int = 0, device="cuda",
+                 norm_weight: torch.Tensor | None = None):
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.x = torch.randn((m, HIDDEN), generator=g, device=device).to(torch.bfloat16)
+        self.w = (norm_weight if norm_weight is not None
+                  else torch.ones(HIDDEN, device=device, dtype=torch.bfloat16))
+        self.layers = make_layers(layers, device=device, generator=g)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.out: torch.Tensor | None = None
+
+    def step(self) -> torch.Tensor:
+        res = self.x
+        q, s, _ = add_rmsnorm_quant(self.x, None, self.w, EPS)
+        h = None
+        for i, layer in enumerate(self.layers):
+            if i:
+                q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
+            lin = layer["qkv_proj"]
+            qkv = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+            q, s = per_token_quant(qkv[:, :HIDDEN])
+            lin = layer["o_proj"]
+            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+            q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
+            lin = layer["gate_up_proj"]
+            gu = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+            q, s = silu_mul_quant(gu)
+            lin = layer["down_proj"]
+            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+        return h
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """Capture one step into a CUDA graph (after a warm-up call on a side stream)."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.step()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self.step()
+        return self.graph
+
+    @property
+    def launches_per_step(self) -> int:
+        return 1 + len(self.layers) * 7 + (len(self.layers) - 1)
+
+    def weight_bytes(self) -> int:
+        return sum(lin.w_t.numel() + lin.scale.numel() * 4 for layer in self.layers
+                   for lin in layer.values())

@@ -1,0 +1,159 @@
+"""The sm_100a W8A8 GEMM against the CPU oracle (oracle/gemm.py).
+
+Mirrors the reference's tests/test_kernel.py: exact int32 products at its shapes,
+other tilings, the 16 scaled-output cases, declines, CUDA-graph replay and odd
+pointers; plus B200-specific coverage (every tile family, stream-K splits, ragged
+M/N/K, bit-exact bf16/fp16 epilogue against the fp32 restatement).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from int8_linear import Config, NotSupported, _native, w8a8_mm
+from int8_linear.kernel import choose_config
+from oracle import gemm as og
+from oracle.numerics import to_bits
+from tests.gpu_util import bits, ints, np_, offset_ints
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1, 2048, 2048), (3, 2048, 1024), (17, 2048, 6144), (64, 2048, 2048), (100, 6144, 2048)]
+
+
+def exact(a: torch.Tensor, w: torch.Tensor) -> np.ndarray:
+    return og.exact(np_(a), np_(w))
+
+
+def one():
+    return torch.ones(1, device="cuda")
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES)
+def test_int32_product_is_exact(m, k, n):
+    a, w = ints((m, k), 1), ints((n, k), 2)
+    got = w8a8_mm(a, w.t(), one(), one(), raw=True)
+    assert got.dtype == torch.int32 and np.array_equal(np_(got), exact(a, w))
+
+
+TILINGS = [Config(t, 128) for t in (16, 32, 64, 128, 256)] + [
+    Config(128, 128, swap_ab=True), Config(128, 128), Config(128, 256),
+    Config(16, 128, split=1), Config(128, 256, split=1), Config(64, 128, stages=2),
+    Config(128, 256, stages=2, group_m=1), Config(32, 128, ctas=7), Config(128, 128, ctas=3),
+]
+
+
+@pytest.mark.parametrize("config", TILINGS, ids=lambda c: c.name)
+def test_exact_under_other_tilings(config):
+    m, k, n = 256, 2048, 1024
+    a, w = ints((m, k), 3), ints((n, k), 4)   # 256 tokens: several token tiles when bm < 256
+    got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=config)
+    assert np.array_equal(np_(got), exact(a, w))
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 16, 1), (5, 48, 77), (130, 1040, 300), (300, 4096, 1000),
+                                   (1000, 2048, 129), (777, 6144, 4096), (2048, 1024, 2048)])
+def test_ragged_shapes_are_exact(m, k, n):
+    """Sizes that are no multiple of any tile: TMA fills zeros past the edges and the
+    epilogue masks the stores."""
+    a, w = ints((m, k), m + k), ints((n, k), n)
+    got = w8a8_mm(a, w.t(), one(), one(), raw=True)
+    assert np.array_equal(np_(got), exact(a, w))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("per_row", [True, False])
+@pytest.mark.parametrize("per_col", [True, False])
+@pytest.mark.parametrize("use_bias", [True, False])
+def test_scaled_output_matches_oracle(dtype, per_row, per_col, use_bias):
+    m, k, n = 37, 2048, 1024
+    a, w = ints((m, k), 5), ints((n, k), 6)
+    g = torch.Generator().manual_seed(7)
+    sa = (torch.rand((m, 1) if per_row else (1,), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1) if per_col else (1,), generator=g) * 1e-2 + 1e-3).cuda()
+    bias = torch.randn(n, generator=g).to(dtype).cuda() if use_bias else None
+    got = w8a8_mm(a, w.t(), sa, sb, dtype, bias)
+    assert got.dtype == dtype
+    acc = exact(a, w)
+    b = np_(bias) if use_bias else None
+    # bit-exact against the fp32 restatement of the reference epilogue
+    want = to_bits(og.epilogue_f32(acc, np_(sa), np_(sb), b),
+                   {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[dtype])
+    assert np.array_equal(bits(got), want)
+    # and within the reference's own 1% rule of the float64 layer
+    term, ref = og.scaled_ref(acc, np_(sa), np_(sb), b)
+    assert og.rel_error(np_(got), term, ref) < 1e-2
+
+
+@pytest.mark.parametrize("m", [1, 16, 17, 64, 256, 300, 1024])
+@pytest.mark.parametrize("k,n", [(2048, 4096), (6144, 2048)])
+def test_decode_and_prefill_bf16_bit_exact(m, k, n):
+    """Every default tile family and split path at Qwen3 widths, bf16 out with bias."""
+    a, w = ints((m, k), 11 + m), ints((n, k), 12)
+    g = torch.Generator().manual_seed(13)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias)
+    want = to_bits(og.epilogue_f32(exact(a, w), np_(sa), np_(sb), np_(bias)), "bf16")
+    assert np.array_equal(bits(got), want)
+
+
+def test_declines_shapes_the_kernel_does_not_take():
+    a, w = ints((4, 100), 8), ints((64, 100), 9)
+    with pytest.raises(NotSupported):
+        w8a8_mm(a, w.t(), one(), one())
+    with pytest.raises(NotSupported):       # N-contiguous [K, N] weight
+        w8a8_mm(ints((4, 128), 1), ints((128, 64), 2), one(), one())
+    with pytest.raises(NotSupported):
+        w8a8_mm(ints((4, 128), 1), ints((64, 128), 2).t(), one().double(), one())
+    with pytest.raises(ValueError):
+        w8a8_mm(ints((4, 128), 1), ints((64, 128), 2).t(), torch.ones(3, device="cuda"), one())
+
+
+def test_replays_inside_a_cuda_graph():
+    m, k, n = 16, 2048, 2048
+    a, w = ints((m, k), 10), ints((n, k), 11)
+    sa = torch.full((m, 1), 1e-2, device="cuda")
+    sb = torch.full((n, 1), 1e-2, device="cuda")
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        w8a8_mm(a, w.t(), sa, sb)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = w8a8_mm(a, w.t(), sa, sb)
+    a.copy_(ints((m, k), 12))  # new input in the same buffer
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(static_out, w8a8_mm(a, w.t(), sa, sb))
+    want = to_bits(og.epilogue_f32(exact(a, w), np_(sa), np_(sb)), "bf16")
+    assert np.array_equal(bits(static_out), want)
+
+
+def test_exact_on_an_odd_pointer_repeatedly():
+    m, k, n = 5, 2048, 1024
+    a, w = offset_ints((m, k), 23), ints((n, k), 24)
+    for _ in range(3):
+        assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True)), exact(a, w))
+
+
+def test_repeated_split_calls_leave_the_workspace_clean():
+    """Stream-K tiles reduce through the workspace and zero it again; many calls with
+    different shapes in a row must each stay exact."""
+    for i, (m, k, n) in enumerate([(1, 2048, 2048), (3, 6144, 2048), (16, 2048, 12288),
+                                   (1, 14336, 4096), (256, 2048, 2048), (1, 2048, 2048)] * 2):
+        a, w = ints((m, k), 30 + i), ints((n, k), 40 + i)
+        assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True)), exact(a, w))
+    assert _native.read_status() == 0
+
+
+def test_empty_batch():
+    out = w8a8_mm(ints((0, 2048), 1), ints((64, 2048), 2).t(), one(), one())
+    assert out.shape == (0, 64)
+
+
+def test_choose_config_is_per_shape():
+    assert choose_config(1, 4096, 2048).swapped and not choose_config(4096, 4096, 2048).swapped
