@@ -1,0 +1,535 @@
+"""Benchmark of the W8A8 hot path on B200, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--model qwen3-1.7b-vllm|llama-3-8b] [--no-standin]
+
+Workload: the per-layer sweep at the Qwen3-1.7B shapes vLLM runs
+(qkv 2048x4096, o_proj 2048x2048, gate_up 2048x12288, down 6144x2048), every M in
+{1,2,4,8,16,17,32,64,128,256,1024,4096}, with and without a bf16 bias.  Inputs are
+generated as in config 0 (bf16 N(0,1) activations and N(0,0.02) weights, quantised per
+row to int8).  One step runs every (layer, M, bias) GEMM R=8 times back to back from a
+CUDA graph, each launch on its own weight copy, so weights are always L2-cold (8 copies
+of every layer, 400 MB, far above the 126 MB L2).  `value` is microseconds per sweep:
+one GEMM of every (layer, M, bias), device time.  `e2e` is the same sweep through the
+public API w8a8_mm, eagerly, with each step's int8 activations and scales copied in
+from pinned host memory and every output copied back.
+
+Under torchrun (N > 1) each rank runs its column shard (N/g output columns) of every
+layer, independently; the NCCL all-gather of the shards is timed separately and
+reported as `allgather_us_per_sweep`.
+
+--impl reference times the reference's CPU implementation of the path (the float64
+torch layer of bench/bench_linear.py:164-165, restated in oracle/gemm.py) on this
+host's cores, on a bounded sample of the same sweep, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "W8A8 GEMM µs & roofline % per (M,K,N); stand-in decode µs/layer at bs 1–128"
+M_SWEEP = [1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 1024, 4096]
+STANDIN_BATCHES = [1, 2, 4, 8, 16, 32, 64, 128]
+COPIES = 8          # weight copies per layer = launches per shape per step (L2-cold)
+L2_BYTES = 126 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="qwen3-1.7b-vllm")
+    ap.add_argument("--no-standin", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--out", default=None, help="also write the JSON line to this file")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        p = {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    # Dense int8 tensor throughput is twice dense bf16 on B200 (4.5 vs 2.25 POPS).
+    p["int8_tops"] = 2.0 * p["bf16_tflops"]
+    return p
+
+
+def layers_for(model: str):
+    from int8_linear.shapes import SHAPES
+
+    names = {"qwen3-1.7b-vllm": ["qkv", "o_proj", "gate_up", "down"],
+             "llama-3-8b": ["qkv", "o_proj", "gate_up", "down"]}[model]
+    return [(nm, k, n) for nm, (_, k, n) in zip(names, SHAPES[model])]
+
+
+def alg_bytes(m, k, n, bias) -> int:
+    """Bytes the GEMM must move at least once: A, W, scales, bias, bf16 output."""
+    return m * k + n * k + 4 * m + 4 * n + (2 * n if bias else 0) + 2 * m * n
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- setup
+def quant_rows_t(x):
+    """Per-row symmetric int8 (the operand generation of bench/bench_linear.py:146-150)."""
+    import torch
+
+    scale = x.float().abs().amax(dim=1, keepdim=True).clamp_min(1e-8) / 127.0
+    return (x.float() / scale).round().clamp(-127, 127).to(torch.int8), scale
+
+
+def build_operands(model, world, rank, dev):
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    layers = []
+    for name, k, n in layers_for(model):
+        assert n % world == 0, f"{name}: N={n} does not split over {world} GPUs"
+        nl = n // world
+        copies = []
+        for _ in range(COPIES):
+            w = (torch.randn((nl, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            wq, ws = quant_rows_t(w)
+            del w
+            copies.append((wq, ws))
+        bias = (torch.randn((nl,), generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        layers.append({"name": name, "k": k, "n": n, "nl": nl, "copies": copies, "bias": bias})
+    acts = {}
+    for k in sorted({lay["k"] for lay in layers}):
+        for m in M_SWEEP:
+            a = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+            acts[(m, k)] = quant_rows_t(a)
+    return layers, acts
+
+
+def sweep_cases(layers):
+    return [(lay, m, bias) for bias in (False, True) for lay in layers for m in M_SWEEP]
+
+
+_SIDE = None
+
+
+def capture(fn):
+    """CUDA graph of fn, after one warm-up call on a side stream (one stream for all
+    captures, so the library keeps a single split-K workspace for them)."""
+    import torch
+
+    global _SIDE
+    if _SIDE is None:
+        _SIDE = torch.cuda.Stream()
+    side = _SIDE
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    return graph
+
+
+def time_graph(graph, windows=5):
+    import torch
+
+    graph.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(windows):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3)
+    return statistics.median(ts)
+
+
+# ------------------------------------------------------------------- our arm
+def run_ours(args, world, rank, dev):
+    import torch
+    import torch.distributed as dist
+
+    from int8_linear import w8a8_mm
+    from int8_linear.kernel import choose_config
+
+    pk = peaks()
+    layers, acts = build_operands(args.model, world, rank, dev)
+    cases = sweep_cases(layers)
+
+    def launcher(lay, m, bias, copies):
+        a_q, a_s = acts[(m, lay["k"])]
+        b = lay["bias"] if bias else None
+
+        def fn():
+            for wq, ws in copies:
+                w8a8_mm(a_q, wq.t(), a_s, ws, torch.bfloat16, b)
+        return fn
+
+    # per-shape graphs: COPIES launches on distinct weight copies (L2-cold)
+    graphs, per_shape = [], []
+    for lay, m, bias in cases:
+        g = capture(launcher(lay, m, bias, lay["copies"]))
+        graphs.append(g)
+    for (lay, m, bias), g in zip(cases, graphs):
+        us = time_graph(g) / COPIES
+        k, n = lay["k"], lay["nl"]
+        by, ops = alg_bytes(m, k, n, bias), 2 * m * n * k
+        t_hbm, t_tc = by / (pk["hbm_gbs"] * 1e3), ops / (pk["int8_tops"] * 1e6)
+        per_shape.append({"layer": lay["name"], "M": m, "K": k, "N": n, "bias": bias, "us": round(us, 3),
+                          "bound": "hbm" if t_hbm >= t_tc else "tensor",
+                          "roof_frac": round(max(t_hbm, t_tc) / us, 4),
+                          "gbs": round(by / us / 1e3, 1), "tops": round(ops / us / 1e6, 1),
+                          "tile": choose_config(m, n, k).name})
+    # L2-warm numbers (the reference's method: the same weight replayed) for the no-bias sweep
+    warm = {}
+    for lay, m, bias in cases:
+        if bias:
+            continue
+        g = capture(launcher(lay, m, False, [lay["copies"][0]] * COPIES))
+        warm[f"{lay['name']}/{m}"] = round(time_graph(g) / COPIES, 3)
+        del g
+
+    # ------------------------------------------------ timed region
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        for g in graphs:
+            g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(dev.index) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            for g in graphs:
+                g.replay()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value_us = ms * 1e3 / COPIES
+
+    # roofline of the GEMM kernel, by the class of launches that takes most of the time
+    cls = {"hbm": [0.0, 0.0], "tensor": [0.0, 0.0]}
+    for row in per_shape:
+        k, n, m = row["K"], row["N"], row["M"]
+        amount = alg_bytes(m, k, n, row["bias"]) if row["bound"] == "hbm" else 2 * m * n * k
+        cls[row["bound"]][0] += amount
+        cls[row["bound"]][1] += row["us"]
+    traffic = None
+    tf = ROOT / "profiles" / "gemm_traffic.json"
+    traffic_map = json.loads(tf.read_text()) if tf.exists() else {}
+
+    def roof(kind):
+        amount, us = cls[kind]
+        if us == 0:
+            return None
+        if kind == "hbm":
+            ach = amount / us / 1e3
+            return {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                    "frac": round(ach / pk["hbm_gbs"], 4), "traffic": traffic_map.get("hbm"),
+                    "time_share": None, "peak_source": pk["source"] + " hbm copy"}
+        ach = amount / us / 1e6
+        return {"bound": "tensor", "achieved": round(ach, 1), "peak": pk["int8_tops"], "unit": "TOPS",
+                "frac": round(ach / pk["int8_tops"], 4), "traffic": traffic_map.get("tensor"),
+                "time_share": None, "peak_source": pk["source"] + " bf16 x2 (dense int8 = 2x bf16)"}
+
+    total_us = cls["hbm"][1] + cls["tensor"][1]
+    main_kind = "hbm" if cls["hbm"][1] >= cls["tensor"][1] else "tensor"
+    roofline, other = roof(main_kind), roof("tensor" if main_kind == "hbm" else "hbm")
+    for r, kind in ((roofline, main_kind), (other, "tensor" if main_kind == "hbm" else "hbm")):
+        if r:
+            r["time_share"] = round(cls[kind][1] / total_us, 3)
+    del traffic
+
+    # ------------------------------------------------ all-gather of column shards
+    allgather_us = None
+    if world > 1:
+        tot = 0.0
+        for lay, m, bias in cases:
+            if bias:
+                continue
+            local = torch.empty((m, lay["nl"]), dtype=torch.bfloat16, device=dev)
+            full = torch.empty((world * m, lay["nl"]), dtype=torch.bfloat16, device=dev)
+            for _ in range(3):
+                dist.all_gather_into_tensor(full, local)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(10):
+                dist.all_gather_into_tensor(full, local)
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b) * 1e3 / 10
+        t = torch.tensor([tot], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        allgather_us = round(float(t.item()), 2)
+
+    # ------------------------------------------------ end to end through the public API
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(layers, acts, cases, dev, world, max(1, min(args.steps, 5)))
+
+    del graphs
+    standin = None
+    if not args.no_standin and world == 1:
+        standin = run_standin(dev)
+
+    launches = args.steps * len(cases) * COPIES
+    return {
+        "value": round(value_us, 2), "ms_per_step": round(ms, 4), "per_shape": per_shape,
+        "l2_warm_us": warm, "roofline": roofline, "roofline_other": other,
+        "allgather_us_per_sweep": allgather_us, "e2e": e2e, "standin_us_per_layer": standin,
+        "clocks": clocks.summary(), "gpu_launches": launches,
+    }
+
+
+def run_e2e(layers, acts, cases, dev, world, passes):
+    """The sweep through w8a8_mm with host buffers: H2D of each case's int8 activations
+    and scales from pinned memory, the GEMM, D2H of the output into pinned memory."""
+    import torch
+    import torch.distributed as dist
+
+    from int8_linear import w8a8_mm
+
+    host = []
+    h2d = d2h = 0
+    for lay, m, bias in cases:
+        a_q, a_s = acts[(m, lay["k"])]
+        ha, hs = a_q.cpu().pin_memory(), a_s.cpu().pin_memory()
+        ho = torch.empty((m, lay["nl"]), dtype=torch.bfloat16).pin_memory()
+        host.append((lay, m, bias, ha, hs, ho))
+        h2d += ha.numel() + hs.numel() * 4
+        d2h += ho.numel() * 2
+    dev_bufs = {id(ha): (torch.empty_like(ha, device=dev), torch.empty_like(hs, device=dev))
+                for _, _, _, ha, hs, _ in host}
+
+    def one_pass():
+        for i, (lay, m, bias, ha, hs, ho) in enumerate(host):
+            da, ds = dev_bufs[id(ha)]
+            da.copy_(ha, non_blocking=True)
+            ds.copy_(hs, non_blocking=True)
+            wq, ws = lay["copies"][i % COPIES]
+            out = w8a8_mm(da, wq.t(), ds, ws, torch.bfloat16, lay["bias"] if bias else None)
+            ho.copy_(out, non_blocking=True)
+
+    one_pass()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(passes):
+        one_pass()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / passes
+    if world > 1:
+        t = torch.tensor([us], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+    return {"value": round(us, 2), "unit": "us", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "passes": passes,
+            "note": "one eager pass over the sweep through int8_linear.w8a8_mm, host copies included"}
+
+
+def run_standin(dev):
+    """28-layer stand-in decode step, one CUDA graph, µs per layer."""
+    import torch
+
+    from int8_linear.standin import LAYERS, StandinDecoder
+
+    out = {}
+    for m in STANDIN_BATCHES:
+        s = StandinDecoder(m, device=dev)
+        g = s.capture()
+        ts = []
+        for _ in range(3):
+            ts.append(time_graph(g, windows=5))
+        out[str(m)] = round(statistics.median(ts) / LAYERS, 2)
+        del g, s
+        torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------- reference arm
+def cpu_sample_pass(model, rng_seed=0, row_cap=256, col_cap=2048, world=1):
+    """One bounded pass of the sweep through the reference's CPU float64 layer
+    (oracle/gemm.py): rows capped at row_cap and columns at col_cap per GEMM, the time
+    scaled by the full/sampled size (the float64 product is linear in M and N).
+    Returns projected microseconds for the whole sweep."""
+    import numpy as np
+
+    from oracle import gemm as og
+    from oracle.numerics import f32_to_bf16_bits
+
+    rng = np.random.default_rng(rng_seed)
+    total = 0.0
+    for bias in (False, True):
+        for name, k, n in layers_for(model):
+            n = n // world
+            nc = min(n, col_cap)
+            w_q = rng.integers(-127, 128, (nc, k), dtype=np.int8)
+            w_s = (rng.random((nc, 1), dtype=np.float32) * 1e-3 + 1e-4).astype(np.float32)
+            b = (rng.standard_normal(nc) * 0.01).astype(np.float32) if bias else None
+            for m in M_SWEEP:
+                mr = min(m, row_cap)
+                a_q = rng.integers(-127, 128, (mr, k), dtype=np.int8)
+                a_s = (rng.random((mr, 1), dtype=np.float32) * 1e-2).astype(np.float32)
+                t0 = time.perf_counter()
+                acc = og.exact(a_q, w_q)
+                _, ref = og.scaled_ref(acc, a_s, w_s, b)
+                f32_to_bf16_bits(ref.astype(np.float32))
+                dt = time.perf_counter() - t0
+                total += dt * (m / mr) * (n / nc)
+    return total * 1e6
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_sample_pass(args.model, world=1)
+    t0 = time.perf_counter()
+    vals = [cpu_sample_pass(args.model, world=1) for _ in range(args.steps)]
+    wall = time.perf_counter() - t0
+    v = statistics.median(vals)
+    sample = ("one pass of the config-1 sweep (96 GEMMs) through the float64 layer, each GEMM "
+              "on at most 256 rows x 2048 columns, time scaled to the full M x N")
+    return {
+        "value": round(v, 1), "ms_per_step": round(wall * 1e3 / args.steps, 2),
+        "cpu_baseline": {"value": round(v, 1), "unit": "us", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(v, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ------------------------------------------------------------------- main
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    base = {"metric": METRIC, "unit": "us", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "data": "synthetic",
+            "config": {"workload": f"per-layer sweep, {args.model} (BASELINE config "
+                                   f"{1 if args.model.startswith('qwen') else 2})",
+                       "layers": [f"{nm} K={k} N={n}" for nm, k, n in layers_for(args.model)],
+                       "M": M_SWEEP, "bias": [False, True],
+                       "l2": f"cold: {COPIES} weight copies per layer rotated, inputs > L2",
+                       "parallelism": f"column-parallel N/{world}" if world > 1 else "single GPU"}}
+    if args.impl == "reference":
+        res = run_reference(args, world, rank)
+        if rank == 0:
+            line = dict(base, impl="reference", dtype="f64", **res)
+            print(json.dumps(line), flush=True)
+        return
+
+    import numpy as np  # noqa: F401  (imported before CUDA so a spawned pool would be safe)
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    res = run_ours(args, world, rank, dev)
+    cpu = None
+    if world == 1 and rank == 0:
+        v = cpu_sample_pass(args.model)
+        cpu = {"value": round(v, 1), "unit": "us", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": "one pass of the sweep through the float64 layer (oracle/gemm.py), each "
+                         "GEMM on at most 256 rows x 2048 columns, time scaled to the full M x N"}
+    if rank == 0:
+        line = dict(base, dtype="i8", cpu_baseline=cpu, **res)
+        print(json.dumps(line), flush=True)
+        if args.out:
+            Path(args.out).write_text(json.dumps(line, indent=1) + "\n")
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

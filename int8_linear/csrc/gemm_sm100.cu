@@ -59,8 +59,9 @@ struct GemmArgs {
   void *out;
   int out_dtype;
   long long ldc;
-  int vec_store;
-  int *ws;        // workspace slots, 128*TN int32 each
+  int vec_store;  // direct-store fallback: 16-byte vector stores allowed
+  int tma_out;    // output written through shared memory by TMA stores
+  int *ws;        // workspace slots, 128*TN int32 each ([TN][128] per slot)
   int *counters;  // one k-block counter per slot
   int *status;
 };
@@ -153,6 +154,20 @@ __device__ __forceinline__ float dequant(int acc, float sa, float sb, float bias
   return v;
 }
 
+// Storage bits of one output value.
+__device__ __forceinline__ uint32_t out_bits16(int dtype, float v) {
+  if (dtype == I8L_BF16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(v);
+    return *reinterpret_cast<uint16_t *>(&h);
+  }
+  __half h = __float2half_rn(v);
+  return *reinterpret_cast<uint16_t *>(&h);
+}
+
+__device__ __forceinline__ uint32_t out_bits32(int dtype, int acc, float v) {
+  return dtype == I8L_I32 ? static_cast<uint32_t>(acc) : __float_as_uint(v);
+}
+
 __device__ __forceinline__ void store_elem(void *out, int dtype, long long idx,
                                            int acc, float v) {
   switch (dtype) {
@@ -171,16 +186,15 @@ __device__ __forceinline__ void store_elem(void *out, int dtype, long long idx,
   }
 }
 
-// Stores 16 accumulator values of one TMEM lane (`row` of the X tile) for the
-// accumulator columns c0..c0+15 (columns of the Y tile).
+// Direct-store fallback (output not TMA-addressable): stores 16 accumulator
+// values of TMEM lane `row` for accumulator columns c0..c0+15 with plain stores.
 template <int TN>
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs &a, int tx, int ty,
-                                               int row, int c0,
-                                               const uint32_t (&r)[16]) {
+__device__ __forceinline__ void epilogue_direct(const GemmArgs &a, int tx, int ty,
+                                                int row, int c0,
+                                                const uint32_t (&r)[16]) {
   const bool raw = a.out_dtype == I8L_I32;
   const bool has_bias = a.bias != nullptr;
   if (a.swap) {
-    // X rows are output columns n, Y rows are tokens m.
     const int n = tx * kXRows + row;
     if (n >= a.N) return;
     const float sb = raw ? 0.f : (a.sb_per_col ? a.sb[n] : a.sb[0]);
@@ -197,57 +211,19 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &a, int tx, int ty
       }
     }
   } else {
-    // X rows are tokens m, Y rows are output columns n.
     const int m = tx * kXRows + row;
     if (m >= a.M) return;
     const int n0 = ty * TN + c0;
     const long long base = static_cast<long long>(m) * a.ldc + n0;
-    if (raw) {
-      if (a.vec_store && n0 + 16 <= a.N) {
-        int4 *dst = reinterpret_cast<int4 *>(static_cast<int *>(a.out) + base);
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4)
-          dst[v4] = make_int4(r[4 * v4], r[4 * v4 + 1], r[4 * v4 + 2], r[4 * v4 + 3]);
-      } else {
-        for (int j = 0; j < 16 && n0 + j < a.N; ++j)
-          static_cast<int *>(a.out)[base + j] = static_cast<int>(r[j]);
-      }
-      return;
-    }
-    const float sa = a.sa_per_row ? a.sa[m] : a.sa[0];
-    float v[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int n = min(n0 + j, a.N - 1);
-      const float sb = a.sb_per_col ? a.sb[n] : a.sb[0];
-      const float bias = has_bias ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f;
-      v[j] = dequant(static_cast<int>(r[j]), sa, sb, bias, has_bias);
-    }
-    if (a.vec_store && n0 + 16 <= a.N) {
-      if (a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16) {
-        uint32_t p[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (a.out_dtype == I8L_BF16) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-            p[j] = *reinterpret_cast<uint32_t *>(&h);
-          } else {
-            __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-            p[j] = *reinterpret_cast<uint32_t *>(&h);
-          }
-        }
-        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.out) + base);
-        dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
-        dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
-      } else {
-        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(a.out) + base);
-#pragma unroll
-        for (int v4 = 0; v4 < 4; ++v4)
-          dst[v4] = make_float4(v[4 * v4], v[4 * v4 + 1], v[4 * v4 + 2], v[4 * v4 + 3]);
-      }
-    } else {
-      for (int j = 0; j < 16 && n0 + j < a.N; ++j)
-        store_elem(a.out, a.out_dtype, base + j, static_cast<int>(r[j]), v[j]);
+    const float sa = raw ? 0.f : (a.sa_per_row ? a.sa[m] : a.sa[0]);
+    for (int j = 0; j < 16 && n0 + j < a.N; ++j) {
+      const int n = n0 + j;
+      const int acc = static_cast<int>(r[j]);
+      float v = 0.f;
+      if (!raw)
+        v = dequant(acc, sa, a.sb_per_col ? a.sb[n] : a.sb[0],
+                    has_bias ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f, has_bias);
+      store_elem(a.out, a.out_dtype, base + j, acc, v);
     }
   }
 }
@@ -257,10 +233,6 @@ template <int TN>
 __device__ __forceinline__ int live_cols(const GemmArgs &a, int ty) {
   const int rows_y = a.swap ? a.M : a.N;
   return min(TN, rows_y - ty * TN);
-}
-
-__device__ __forceinline__ void red_add_s32(int *p, int v) {
-  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ int ld_cg_s32(const int *p) {
@@ -273,22 +245,140 @@ __device__ __forceinline__ void st_cg_s32(int *p, int v) {
   asm volatile("st.global.cg.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+constexpr int kStageBufBytes = 2048;                            // one staging buffer
+constexpr int kStagingBytes = kEpiWarps * 2 * kStageBufBytes;   // 16 KB
+constexpr int kScalFloats = 256;                                // per array per buffer
+constexpr int kScalBytes = 2 * 2 * kScalFloats * 4;             // [2 arrays][2 acc][256]
+
 template <int TN>
 struct SmemLayout {
   static constexpr int kYBytes = TN * kBK;
   static constexpr int kStageBytes = kXBytes + kYBytes;
   static constexpr int kTmemCols = (2 * TN < 32) ? 32 : 2 * TN;
-  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain, + tmem slot, flags
+  // stages | staging | scales | barriers: full[S], empty[S], acc_full[2],
+  // acc_empty[2], drain | tmem slot, flags
   static size_t bytes(int stages) {
     return 1024 /* alignment slack */ + static_cast<size_t>(stages) * kStageBytes +
-           static_cast<size_t>(2 * stages + 5) * 8 + 64;
+           kStagingBytes + kScalBytes + static_cast<size_t>(2 * stages + 5) * 8 + 64;
   }
 };
+
+// A warp's two 2 KB staging buffers for TMA stores / reduces; lane 0 owns the
+// bulk groups.  acquire() returns a buffer no bulk operation still reads.
+struct Staging {
+  uint8_t *base;
+  uint32_t count;
+
+  __device__ __forceinline__ uint8_t *acquire(int lane) {
+    if (count >= 2 && lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    uint8_t *b = base + (count & 1u) * kStageBufBytes;
+    ++count;
+    return b;
+  }
+
+  __device__ __forceinline__ void drain(int lane) {
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+};
+
+// Everything one epilogue thread needs about the current tile.
+struct TileCtx {
+  int tx, ty, ncols;
+  uint32_t taddr;     // TMEM address of this warp's lanes in the accumulator
+  const float *s_col; // per accumulator column: sb (normal) or sa (swap), smem
+  const float *b_col; // per accumulator column: bias (normal), smem
+  float s_row, b_row; // per TMEM lane: sa (normal) or sb, bias (swap)
+};
+
+// Writes 16 values (columns c0..c0+15 of this thread's TMEM lane) through the
+// staging buffer and a TMA store.  Swap: box {32 n, 16 m}.
+template <int TN>
+__device__ __forceinline__ void emit_swap16(const GemmArgs &a, const CUtensorMap *map_out,
+                                            const TileCtx &t, int quarter, int lane, int c0,
+                                            const uint32_t (&r)[16], Staging &st) {
+  uint8_t *buf = st.acquire(lane);
+  const bool raw = a.out_dtype == I8L_I32;
+  const bool has_bias = a.bias != nullptr;
+  if (a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16) {
+    uint16_t *b16 = reinterpret_cast<uint16_t *>(buf);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float v = dequant(static_cast<int>(r[j]), t.s_col[c0 + j], t.s_row, t.b_row, has_bias);
+      b16[j * 32 + lane] = static_cast<uint16_t>(out_bits16(a.out_dtype, v));
+    }
+  } else {
+    uint32_t *b32 = reinterpret_cast<uint32_t *>(buf);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int acc = static_cast<int>(r[j]);
+      const float v = raw ? 0.f : dequant(acc, t.s_col[c0 + j], t.s_row, t.b_row, has_bias);
+      b32[j * 32 + lane] = out_bits32(a.out_dtype, acc, v);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const int n0 = t.tx * kXRows + quarter * 32, m0 = t.ty * TN + c0;
+    if (n0 < a.N && m0 < a.M) tma_store_2d(map_out, buf, n0, m0);  // skip boxes wholly outside
+    bulk_commit();
+  }
+}
+
+// Normal orientation: one 64-byte-per-row subtile (32 columns of a 16-bit
+// output from r0 and r1, or 16 columns of a 32-bit output from r0), written
+// with the 64-byte swizzle the output tensor map uses.  Box {cols, 32 m}.
+template <int TN>
+__device__ __forceinline__ void emit_normal(const GemmArgs &a, const CUtensorMap *map_out,
+                                            const TileCtx &t, int quarter, int lane, int c0,
+                                            const uint32_t (&r0)[16], const uint32_t (&r1)[16],
+                                            Staging &st) {
+  uint8_t *buf = st.acquire(lane);
+  const bool raw = a.out_dtype == I8L_I32;
+  const bool has_bias = a.bias != nullptr;
+  uint32_t p[16];
+  if (a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int ca = c0 + 2 * j;
+      const float v0 = dequant(static_cast<int>(r0[2 * j]), t.s_row, t.s_col[ca], t.b_col[ca], has_bias);
+      const float v1 = dequant(static_cast<int>(r0[2 * j + 1]), t.s_row, t.s_col[ca + 1], t.b_col[ca + 1], has_bias);
+      p[j] = out_bits16(a.out_dtype, v0) | (out_bits16(a.out_dtype, v1) << 16);
+      const int cb = c0 + 16 + 2 * j;
+      const float w0 = dequant(static_cast<int>(r1[2 * j]), t.s_row, t.s_col[cb], t.b_col[cb], has_bias);
+      const float w1 = dequant(static_cast<int>(r1[2 * j + 1]), t.s_row, t.s_col[cb + 1], t.b_col[cb + 1], has_bias);
+      p[8 + j] = out_bits16(a.out_dtype, w0) | (out_bits16(a.out_dtype, w1) << 16);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int acc = static_cast<int>(r0[j]);
+      const float v = raw ? 0.f : dequant(acc, t.s_row, t.s_col[c0 + j], t.b_col[c0 + j], has_bias);
+      p[j] = out_bits32(a.out_dtype, acc, v);
+    }
+  }
+  uint8_t *rowp = buf + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4 *>(rowp + ((c ^ sw) << 4)) =
+        make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const int n0 = t.ty * TN + c0, m0 = t.tx * kXRows + quarter * 32;
+    if (n0 < a.N && m0 < a.M) tma_store_2d(map_out, buf, n0, m0);  // skip boxes wholly outside
+    bulk_commit();
+  }
+}
 
 template <int TN>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_gemm_sm100(const __grid_constant__ CUtensorMap map_x,
-                    const __grid_constant__ CUtensorMap map_y, const GemmArgs a) {
+                    const __grid_constant__ CUtensorMap map_y,
+                    const __grid_constant__ CUtensorMap map_out,
+                    const __grid_constant__ CUtensorMap map_ws, const GemmArgs a) {
   using L = SmemLayout<TN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -296,7 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int S = a.stages;
   uint8_t *sx = smem;
   uint8_t *sy = smem + static_cast<size_t>(S) * kXBytes;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + static_cast<size_t>(S) * L::kStageBytes);
+  uint8_t *staging = smem + static_cast<size_t>(S) * L::kStageBytes;
+  float *scal = reinterpret_cast<float *>(staging + kStagingBytes);
+  uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(scal) + kScalBytes);
   uint64_t *empty = full + S;
   uint64_t *acc_full = empty + S;
   uint64_t *acc_empty = acc_full + 2;
@@ -326,6 +418,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&map_x);
     tma_prefetch_desc(&map_y);
   }
+  if (warp == 2 && lane == 0) {
+    if (a.tma_out) tma_prefetch_desc(&map_out);
+    if (a.sk_iters > 0) tma_prefetch_desc(&map_ws);
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
@@ -339,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_x = a.swap ? policy_evict_first() : policy_evict_last();
-      const uint64_t pol_y = a.swap ? policy_evict_last() : policy_evict_last();
+      const uint64_t pol_y = policy_evict_last();
       Schedule sch;
       sch.init(a);
       Segment seg;
@@ -442,47 +538,123 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const int epi_tid = threadIdx.x - 64;
+    const bool raw = a.out_dtype == I8L_I32;
+    const bool has_bias = a.bias != nullptr;
+    const bool wide = a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16;
+    Staging st{staging + static_cast<size_t>(quarter) * 2 * kStageBufBytes, 0u};
     Schedule sch;
     sch.init(a);
     Segment seg;
     int acc = 0;
     uint32_t acc_phase = 0;
     while (sch.next(a, seg)) {
+      TileCtx t;
+      tile_coords(a, seg.tile, t.tx, t.ty);
+      t.ncols = live_cols<TN>(a, t.ty);
+      t.taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * TN);
+      // Scales and bias for this tile, fetched before the accumulator is ready.
+      float *s_col = scal + acc * kScalFloats;
+      float *b_col = scal + 2 * kScalFloats + acc * kScalFloats;
+      t.s_col = s_col;
+      t.b_col = b_col;
+      t.s_row = 0.f;
+      t.b_row = 0.f;
+      if (!raw) {
+        if (a.swap) {
+          const int n = t.tx * kXRows + row;
+          if (n < a.N) {
+            t.s_row = a.sb_per_col ? a.sb[n] : a.sb[0];
+            t.b_row = has_bias ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f;
+          }
+          for (int c = epi_tid; c < TN; c += kEpiWarps * 32) {
+            const int m = t.ty * TN + c;
+            s_col[c] = m < a.M ? (a.sa_per_row ? a.sa[m] : a.sa[0]) : 0.f;
+          }
+        } else {
+          const int m = t.tx * kXRows + row;
+          if (m < a.M) t.s_row = a.sa_per_row ? a.sa[m] : a.sa[0];
+          for (int c = epi_tid; c < TN; c += kEpiWarps * 32) {
+            const int n = t.ty * TN + c;
+            s_col[c] = n < a.N ? (a.sb_per_col ? a.sb[n] : a.sb[0]) : 0.f;
+            b_col[c] = (has_bias && n < a.N) ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f;
+          }
+        }
+      }
       const bool ok = mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, a.status,
                                         kStatusEpilogueWait);
-      // All four epilogue warps continue or all stop: they meet at named barriers below.
+      // All four epilogue warps continue or all stop: they meet at named barriers
+      // below.  The barrier also publishes the scale arrays written above.
       if (!named_bar_and(2, kEpiWarps * 32, ok)) break;
       tc_fence_after();
-      int tx, ty;
-      tile_coords(a, seg.tile, tx, ty);
-      const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * TN);
-      const int ncols = live_cols<TN>(a, ty);
       const bool whole = seg.kb0 == 0 && seg.kb1 == a.kblocks;
       if (whole) {
-        for (int c0 = 0; c0 < ncols; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c0, r);
-          tmem_ld_wait();
-          epilogue_chunk<TN>(a, tx, ty, row, c0, r);
+        if (!a.tma_out) {
+          for (int c0 = 0; c0 < t.ncols; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(t.taddr + c0, r);
+            tmem_ld_wait();
+            epilogue_direct<TN>(a, t.tx, t.ty, row, c0, r);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        } else if (a.swap) {
+          for (int c0 = 0; c0 < t.ncols; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(t.taddr + c0, r);
+            tmem_ld_wait();
+            if (c0 + 16 >= t.ncols) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            emit_swap16<TN>(a, &map_out, t, quarter, lane, c0, r, st);
+          }
+        } else {
+          const int step = wide ? 32 : 16;
+          for (int c0 = 0; c0 < t.ncols; c0 += step) {
+            uint32_t r0[16], r1[16];
+            tmem_ld16(t.taddr + c0, r0);
+            if (wide) tmem_ld16(t.taddr + c0 + 16, r1);
+            tmem_ld_wait();
+            if (c0 + step >= t.ncols) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            emit_normal<TN>(a, &map_out, t, quarter, lane, c0, r0, r1, st);
+          }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
       } else {
+        // A piece of a split tile: add it into the tile's workspace slot in L2
+        // (TMA reduce-add of int32 boxes {32 rows, 16 columns}).
         const int slot = split_slot(a, seg.tile);
-        int *ws = a.ws + static_cast<size_t>(slot) * (kXRows * TN);
-        for (int c0 = 0; c0 < ncols; c0 += 16) {
+        for (int c0 = 0; c0 < t.ncols; c0 += 16) {
           uint32_t r[16];
-          tmem_ld16(taddr + c0, r);
+          tmem_ld16(t.taddr + c0, r);
           tmem_ld_wait();
+          if (c0 + 16 >= t.ncols) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          }
+          uint8_t *buf = st.acquire(lane);
+          uint32_t *b32 = reinterpret_cast<uint32_t *>(buf);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) red_add_s32(ws + (c0 + j) * kXRows + row, static_cast<int>(r[j]));
+          for (int j = 0; j < 16; ++j) b32[j * 32 + lane] = r[j];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(&map_ws, buf, quarter * 32, slot * TN + c0);
+            bulk_commit();
+          }
         }
-        tc_fence_before();
+        if (lane == 0) {
+          bulk_wait<0>();
+          fence_proxy_async_global();
+          __threadfence();
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        __threadfence();
         named_bar_sync(1, kEpiWarps * 32);
         if (epi_tid == 0) {
           const int mine = seg.kb1 - seg.kb0;
@@ -491,16 +663,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_bar_sync(1, kEpiWarps * 32);
         if (*last_flag) {
+          // This piece completed the tile: read the sums, store, zero the slot.
           __threadfence();
-          for (int c0 = 0; c0 < ncols; c0 += 16) {
-            uint32_t r[16];
+          int *ws = a.ws + static_cast<size_t>(slot) * (kXRows * TN);
+          const int step = (!a.swap && wide && a.tma_out) ? 32 : 16;
+          for (int c0 = 0; c0 < t.ncols; c0 += step) {
+            uint32_t r0[16], r1[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               int *p = ws + (c0 + j) * kXRows + row;
-              r[j] = static_cast<uint32_t>(ld_cg_s32(p));
+              r0[j] = static_cast<uint32_t>(ld_cg_s32(p));
               st_cg_s32(p, 0);
             }
-            epilogue_chunk<TN>(a, tx, ty, row, c0, r);
+            if (step == 32) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                int *p = ws + (c0 + 16 + j) * kXRows + row;
+                r1[j] = static_cast<uint32_t>(ld_cg_s32(p));
+                st_cg_s32(p, 0);
+              }
+            }
+            if (!a.tma_out)
+              epilogue_direct<TN>(a, t.tx, t.ty, row, c0, r0);
+            else if (a.swap)
+              emit_swap16<TN>(a, &map_out, t, quarter, lane, c0, r0, st);
+            else
+              emit_normal<TN>(a, &map_out, t, quarter, lane, c0, r0, r1, st);
           }
           if (epi_tid == 0) atomicExch(a.counters + slot, 0);
         }
@@ -510,6 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    st.drain(lane);
   }
 
   tc_fence_before();
@@ -561,10 +750,33 @@ static int make_operand_map(CUtensorMap *map, const int8_t *ptr, int64_t rows, i
   return I8L_OK;
 }
 
+// Tensor map over a row-major 2-D matrix of `rows` x `cols` elements (row stride
+// `ld_bytes`), boxes of box_cols x box_rows.
+static int make_map(CUtensorMap *map, CUtensorMapDataType type, const void *ptr, int64_t rows,
+                    int64_t cols, int64_t ld_bytes, int box_cols, int box_rows,
+                    CUtensorMapSwizzle swizzle, const char *what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(I8L_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, type, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(I8L_ECUDA, "cuTensorMapEncodeTiled failed (CUresult %d) for the %s map [%lld x %lld]",
+                     static_cast<int>(r), what, static_cast<long long>(rows),
+                     static_cast<long long>(cols));
+  return I8L_OK;
+}
+
+static size_t smem_extra() { return 1024 + kStagingBytes + kScalBytes + 5 * 8 + 64; }
+
 static int max_stages_for(int tn, int smem_optin) {
   const int stage = kXBytes + tn * kBK;
-  const int avail = smem_optin - 1024 - 256;
-  return std::max(1, std::min(16, avail / stage));
+  const int avail = smem_optin - static_cast<int>(smem_extra()) - 16;
+  return std::max(1, std::min(16, avail / (stage + 16)));
 }
 
 static bool valid_tok_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128 || t == 256; }
@@ -659,8 +871,9 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
 }
 
 template <int TN>
-static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const GemmArgs &a, int ctas,
-                     int stages, cudaStream_t stream) {
+static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const CUtensorMap &mo,
+                     const CUtensorMap &mw, const GemmArgs &a, int ctas, int stages,
+                     cudaStream_t stream) {
   const size_t smem = SmemLayout<TN>::bytes(stages);
   // Largest dynamic shared memory already allowed, per device (the attribute is
   // set on the function as loaded in each device's context).
@@ -674,7 +887,7 @@ static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const GemmArg
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
-  w8a8_gemm_sm100<TN><<<ctas, kThreads, smem, stream>>>(mx, my, a);
+  w8a8_gemm_sm100<TN><<<ctas, kThreads, smem, stream>>>(mx, my, mo, mw, a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "gemm launch");
   return I8L_OK;
@@ -765,25 +978,46 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   a.out_dtype = out_dtype;
   a.ldc = ldc;
   const int esize = (out_dtype == I8L_BF16 || out_dtype == I8L_F16) ? 2 : 4;
-  a.vec_store = (reinterpret_cast<uintptr_t>(out) % 16 == 0 && (ldc * esize) % 16 == 0) ? 1 : 0;
+  const bool aligned_out = reinterpret_cast<uintptr_t>(out) % 16 == 0 && (ldc * esize) % 16 == 0;
+  a.vec_store = aligned_out ? 1 : 0;
+  CUtensorMap mo{}, mw{};
+  if (aligned_out) {
+    static const CUtensorMapDataType kTypes[4] = {
+        CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+        CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_DATA_TYPE_INT32};
+    // swap: boxes of 32 output columns x 16 tokens; else 64 bytes of columns x 32 rows.
+    if (swap)
+      e = make_map(&mo, kTypes[out_dtype], out, M, N, ldc * esize, 32, 16,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, "output");
+    else
+      e = make_map(&mo, kTypes[out_dtype], out, M, N, ldc * esize, 64 / esize, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B, "output");
+    if (e) return e;
+    a.tma_out = 1;
+  }
   if (p.ws_bytes) {
     const size_t counters_bytes = ((static_cast<size_t>(p.slots) * 4 + 255) / 256) * 256;
     a.counters = static_cast<int *>(workspace);
     a.ws = reinterpret_cast<int *>(static_cast<uint8_t *>(workspace) + counters_bytes);
+    // [slots * TN columns][128 rows] int32, reduced into in boxes of 32 rows x 16 columns.
+    if ((e = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, a.ws,
+                      static_cast<int64_t>(p.slots) * p.tn, kXRows, kXRows * 4, 32, 16,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, "workspace")))
+      return e;
   }
   a.status = status_ptr();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (p.tn) {
     case 16:
-      return launch_tn<16>(mx, my, a, p.ctas, a.stages, s);
+      return launch_tn<16>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     case 32:
-      return launch_tn<32>(mx, my, a, p.ctas, a.stages, s);
+      return launch_tn<32>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     case 64:
-      return launch_tn<64>(mx, my, a, p.ctas, a.stages, s);
+      return launch_tn<64>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     case 128:
-      return launch_tn<128>(mx, my, a, p.ctas, a.stages, s);
+      return launch_tn<128>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     case 256:
-      return launch_tn<256>(mx, my, a, p.ctas, a.stages, s);
+      return launch_tn<256>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     default:
       return set_error(I8L_ENOTSUP, "no kernel for tile width %d", p.tn);
   }

@@ -54,7 +54,8 @@ def test_exact_under_other_tilings(config):
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 16, 1), (5, 48, 77), (130, 1040, 300), (300, 4096, 1000),
-                                   (1000, 2048, 129), (777, 6144, 4096), (2048, 1024, 2048)])
+                                   (1000, 2048, 129), (777, 6144, 4096), (2048, 1024, 2048),
+                                   (5, 2048, 1040), (300, 2048, 1040), (40, 512, 1048)])
 def test_ragged_shapes_are_exact(m, k, n):
     """Sizes that are no multiple of any tile: TMA fills zeros past the edges and the
     epilogue masks the stores."""
@@ -148,6 +149,22 @@ def test_repeated_split_calls_leave_the_workspace_clean():
         a, w = ints((m, k), 30 + i), ints((n, k), 40 + i)
         assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True)), exact(a, w))
     assert _native.read_status() == 0
+
+
+@pytest.mark.parametrize("m,n", [(1, 1040), (37, 1000), (300, 1040), (513, 2056), (200, 136)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_edge_tiles_bit_exact(m, n, dtype):
+    """Output tiles that hang over M and N (some warps' store boxes lie wholly outside)."""
+    k = 1024
+    a, w = ints((m, k), 50 + m), ints((n, k), 51)
+    g = torch.Generator().manual_seed(52)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = torch.randn(n, generator=g).to(dtype).cuda()
+    got = w8a8_mm(a, w.t(), sa, sb, dtype, bias)
+    want = to_bits(og.epilogue_f32(exact(a, w), np_(sa), np_(sb), np_(bias)),
+                   "bf16" if dtype == torch.bfloat16 else "f32")
+    assert np.array_equal(bits(got), want)
 
 
 def test_empty_batch():
