@@ -92,6 +92,36 @@ int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
                 size_t ws_bytes, void *stream);
 
 /*
+ * i8l_w8a8_mm for callers that cannot allocate device memory.  No counterpart in
+ * the reference (its Triton kernel needed no scratch).
+ *
+ * Who needs it: a host that owns all device memory through a fixed arena and forbids
+ * allocation inside its execute callback, a latency-critical path that must not run
+ * into cudaMalloc's implicit device synchronisation, or a caller from another
+ * language with no allocator binding.  The caller still passes the inputs and the
+ * output; only the split-K scratch changes: it is a fixed array of
+ * I8L_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU that loads the
+ * library holds until the process exits.  This call allocates nothing.
+ *
+ * - A problem whose scratch (i8l_workspace_size for the same tile) exceeds
+ *   I8L_NOALLOC_SCRATCH_BYTES is rejected with I8L_EWORKSPACE and a message naming
+ *   both sizes; a tile with split = 1 needs no scratch.  With the default tiles,
+ *   decode batches up to 64 tokens fit.
+ * - The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress) with that device current; make that first call before
+ *   any stream capture.
+ * - Every call on a device shares the one array and clears the part it needs before
+ *   its kernel runs, so calls whose GPU work overlaps (other streams, other host
+ *   threads, graph branches) race: serialise them.
+ */
+#define I8L_NOALLOC_SCRATCH_BYTES (8u << 20)
+int i8l_w8a8_mm_noalloc(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
+                        const float *sa, int32_t sa_per_row, const float *sb,
+                        int32_t sb_per_col, const void *bias, int32_t bias_dtype,
+                        void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
+                        int32_t K, const i8l_tile *tile, void *stream);
+
+/*
  * Bytes of workspace i8l_w8a8_mm needs for this problem and tile (tile may be
  * NULL for the library's choice).  Host-only, no CUDA calls beyond a cached
  * device-property query.  Replaces nothing in the reference (Triton's kernel kept

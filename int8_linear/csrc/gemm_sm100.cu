@@ -1022,3 +1022,77 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
       return set_error(I8L_ENOTSUP, "no kernel for tile width %d", p.tn);
   }
 }
+
+// ------------------------------------------------------------------ no-allocation entry
+//
+// Some callers cannot allocate device memory at the point where they run a GEMM: a
+// host that owns all device memory through its own fixed arena and forbids
+// allocation inside its execute callback, code that must not hit cudaMalloc's
+// implicit device synchronisation on a latency-critical path, or a foreign-language
+// caller with no binding to an allocator.  For them, i8l_w8a8_mm_noalloc takes its
+// split-K scratch from a fixed array compiled into this library.
+//
+// The array is a file-scope __device__ variable: every GPU that loads the library
+// holds kNoAllocScratchBytes of it until the process exits.  Host code cannot use the
+// array's name as a device address (on the host it is only a stand-in symbol), so the
+// device address is looked up once per device with cudaGetSymbolAddress, with that
+// device current, on the first call made on it.
+
+namespace i8l {
+
+constexpr size_t kNoAllocScratchBytes = I8L_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_addr[64];
+
+// Device address of g_noalloc_scratch on the current device (resolved on first use).
+static int noalloc_scratch(void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return set_error(I8L_EINVAL, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return I8L_OK;
+}
+
+}  // namespace i8l
+
+extern "C" int i8l_w8a8_mm_noalloc(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
+                                   const float *sa, int32_t sa_per_row, const float *sb,
+                                   int32_t sb_per_col, const void *bias, int32_t bias_dtype,
+                                   void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
+                                   int32_t K, const i8l_tile *tile, void *stream) {
+  if (M < 0 || N < 0 || K < 0) return set_error(I8L_EINVAL, "negative size M=%d N=%d K=%d", M, N, K);
+  // Scratch this problem needs under this tile (host arithmetic only).
+  size_t need = 0;
+  if (M > 0 && N > 0 && K > 0 && K % 16 == 0) {
+    Plan p;
+    if (make_plan(M, N, K, tile, &p) == I8L_OK) need = p.ws_bytes;
+  }
+  if (need > kNoAllocScratchBytes)
+    return set_error(I8L_EWORKSPACE,
+                     "i8l_w8a8_mm_noalloc: this problem needs %zu bytes of split-K scratch, more "
+                     "than the library's fixed %zu; pass a tile with split=1 (no scratch) or call "
+                     "i8l_w8a8_mm with a workspace",
+                     need, kNoAllocScratchBytes);
+  void *ws = nullptr;
+  int e = noalloc_scratch(&ws);
+  if (e) return e;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The counters and partial-sum slots must start at zero.  Kernels leave them
+  // zeroed, but a call that ended in an error may not have: clear them every call.
+  if (need) {
+    cudaError_t ce = cudaMemsetAsync(ws, 0, need, s);
+    if (ce != cudaSuccess) return cuda_error(ce, "cudaMemsetAsync(no-alloc scratch)");
+  }
+  return i8l_w8a8_mm(A, lda, W, ldw, sa, sa_per_row, sb, sb_per_col, bias, bias_dtype, out,
+                     out_dtype, ldc, M, N, K, tile, ws, kNoAllocScratchBytes, stream);
+}
