@@ -55,6 +55,7 @@ def parse():
     ap.add_argument("--model", default="qwen3-1.7b-vllm")
     ap.add_argument("--no-standin", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--out", default=None, help="also write the JSON line to this file")
     return ap.parse_args()
 
@@ -498,7 +499,8 @@ def main():
                        "layers": [f"{nm} K={k} N={n}" for nm, k, n in layers_for(args.model)],
                        "M": M_SWEEP, "bias": [False, True],
                        "l2": f"cold: {COPIES} weight copies per layer rotated, inputs > L2",
-                       "parallelism": f"column-parallel N/{world}" if world > 1 else "single GPU"}}
+                       "parallelism": f"column-parallel N/{world}" if world > 1 else "single GPU",
+                       "pdl": not args.no_pdl}}
     if args.impl == "reference":
         res = run_reference(args, world, rank)
         if rank == 0:
@@ -512,6 +514,9 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    from int8_linear import set_pdl
+
+    set_pdl(not args.no_pdl)  # inference weights are read-only: let kernels overlap
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     res = run_ours(args, world, rank, dev)

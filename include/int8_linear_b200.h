@@ -49,8 +49,13 @@ extern "C" {
  *   stages:      shared-memory ring depth (0 = the most that fits);
  *   ctas:        persistent CTAs (0 = one per SM);
  *   group:       tiles walked together along the 128-row side for L2 reuse (>=1);
- *   split:       0 = stream-K over the SMs (tiles may be split along K and the int32
- *                partial sums reduced exactly through the workspace), 1 = whole tiles.
+ *   split:       how K is shared out (int32 partial sums are always reduced exactly):
+ *                0 = the library's choice; 1 = whole tiles; 2 = stream-K over the SMs,
+ *                partial sums reduced through the workspace; 3 = cluster split-K:
+ *                the CTAs of a thread-block cluster split one tile's K and reduce over
+ *                distributed shared memory (swap_ab tiles of up to 64 tokens; no
+ *                workspace);
+ *   cluster:     CTAs per cluster for split = 3 (0 = the library's choice, <= 8).
  */
 typedef struct i8l_tile {
   int32_t swap_ab;
@@ -60,7 +65,7 @@ typedef struct i8l_tile {
   int32_t ctas;
   int32_t group;
   int32_t split;
-  int32_t reserved;
+  int32_t cluster;
 } i8l_tile;
 
 /*
@@ -188,6 +193,18 @@ const char *i8l_last_error(void);
  */
 int i8l_read_status(int32_t *status_out);
 int i8l_clear_status(void);
+
+/*
+ * Programmatic dependent launch (process-wide, off by default).  When on, every kernel
+ * of the library is launched so that it may start while the previous kernel in the
+ * stream is still running: it sets up, and a GEMM loads the weight tiles of its first
+ * pipeline stages, then waits for the previous kernel before reading activations or
+ * scales or writing anything.  Only turn it on when weights (W, sb, bias, norm gamma)
+ * are never written by the kernel launched just before (true for inference).
+ * No reference counterpart (Triton launches are stream-ordered).
+ */
+int i8l_set_pdl(int32_t enable);
+int32_t i8l_get_pdl(void);
 
 /* Library version string and the compiled target, e.g. "0.1.0 sm_100a". */
 const char *i8l_version(void);

@@ -8,6 +8,7 @@ RuntimeError, exactly as the reference's launchers raise them.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -25,7 +26,7 @@ class I8LTile(ctypes.Structure):
     """Mirror of struct i8l_tile."""
 
     _fields_ = [(name, ctypes.c_int32) for name in (
-        "swap_ab", "tok_tile", "w_tile", "stages", "ctas", "group", "split", "reserved")]
+        "swap_ab", "tok_tile", "w_tile", "stages", "ctas", "group", "split", "cluster")]
 
 
 _lib = None
@@ -50,6 +51,8 @@ SIGNATURES = {
     "i8l_read_status": (_i32, [ctypes.POINTER(_i32)]),
     "i8l_clear_status": (_i32, []),
     "i8l_version": (ctypes.c_char_p, []),
+    "i8l_set_pdl": (_i32, [_i32]),
+    "i8l_get_pdl": (_i32, []),
 }
 
 
@@ -73,6 +76,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
             fn.argtypes = args
         if path is None:
             _lib = lib
+            if os.environ.get("INT8_LINEAR_PDL") == "1":
+                lib.i8l_set_pdl(1)
         return lib
 
 
@@ -97,3 +102,14 @@ def read_status() -> int:
 
 def clear_status() -> None:
     check(load().i8l_clear_status())
+
+
+def set_pdl(enable: bool) -> None:
+    """Launch every kernel with programmatic dependent launch (see i8l_set_pdl): a kernel
+    may start while the previous one in the stream runs, and GEMMs prefetch weight tiles
+    before waiting for it.  Only for weights that the preceding kernel never writes."""
+    check(load().i8l_set_pdl(1 if enable else 0))
+
+
+def pdl_enabled() -> bool:
+    return bool(load().i8l_get_pdl())

@@ -1,5 +1,6 @@
 // Shared C-ABI plumbing: per-thread error messages, the cached device query and
 // the device status word that kernels with bounded waits write to.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -15,6 +16,9 @@ namespace i8l {
 __device__ int g_status;
 
 static thread_local char t_err[512] = "no error";
+static std::atomic<int> g_pdl{0};
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
 int set_error(int code, const char *fmt, ...) {
   va_list ap;
@@ -98,3 +102,10 @@ extern "C" int i8l_clear_status(void) {
 }
 
 extern "C" const char *i8l_version(void) { return "0.1.0 sm_100a"; }
+
+extern "C" int i8l_set_pdl(int32_t enable) {
+  g_pdl.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return I8L_OK;
+}
+
+extern "C" int32_t i8l_get_pdl(void) { return g_pdl.load(std::memory_order_relaxed); }

@@ -21,6 +21,7 @@ enum StatusBits : int {
   kStatusEpilogueWait = 1 << 2,
   kStatusDrainWait = 1 << 3,
   kStatusSelfTest = 1 << 4,
+  kStatusClusterWait = 1 << 5,
 };
 
 // A wait that should take microseconds gives up after this many nanoseconds
@@ -90,6 +91,75 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        if (status) atomicOr(status, bit);
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of all CTAs of the cluster; orders shared-memory writes before the
+// barrier with reads after it, cluster-wide.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+// Asynchronous 16-byte store into another CTA's shared memory; its bytes complete
+// the transaction count of that CTA's mbarrier `cluster_bar`.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint4 v, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          cluster_addr),
+      "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(cluster_bar)
+      : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope:
+// this thread's earlier shared-memory writes are visible to the waiter).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (arrivals come from other CTAs).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity,
+                                                          volatile int *abort, int *status,
+                                                          int bit) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -260,6 +330,18 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
   return (2u << 4) | (1u << 7) | (1u << 10) |
          (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue now / wait until the previous kernel finished and its writes are
+// visible.  Both are no-ops for a launch without the programmatic attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- barriers

@@ -64,6 +64,7 @@ struct GemmArgs {
   int *ws;        // workspace slots, 128*TN int32 each ([TN][128] per slot)
   int *counters;  // one k-block counter per slot
   int *status;
+  int cluster;    // >1: the CTAs of each cluster split K of one tile (reduced over DSMEM)
 };
 
 struct Segment {
@@ -78,6 +79,14 @@ struct Schedule {
   long long it, it_end;
 
   __device__ __forceinline__ void init(const GemmArgs &a) {
+    if (a.cluster > 1) {
+      // One tile per cluster; CTA rank r takes the r-th of `cluster` equal k ranges.
+      const int r = static_cast<int>(blockIdx.x) % a.cluster;
+      dp_next = static_cast<int>(blockIdx.x) / a.cluster;
+      it = static_cast<long long>(a.kblocks) * r / a.cluster;
+      it_end = static_cast<long long>(a.kblocks) * (r + 1) / a.cluster;
+      return;
+    }
     dp_next = blockIdx.x;
     const long long g = gridDim.x;
     it = a.sk_iters * static_cast<long long>(blockIdx.x) / g;
@@ -85,6 +94,14 @@ struct Schedule {
   }
 
   __device__ __forceinline__ bool next(const GemmArgs &a, Segment &s) {
+    if (a.cluster > 1) {
+      if (dp_next < 0) return false;
+      s.tile = dp_next;
+      s.kb0 = static_cast<int>(it);
+      s.kb1 = static_cast<int>(it_end);
+      dp_next = -1;
+      return true;
+    }
     if (dp_next < a.dp_tiles) {
       s.tile = dp_next;
       s.kb0 = 0;
@@ -256,10 +273,10 @@ struct SmemLayout {
   static constexpr int kStageBytes = kXBytes + kYBytes;
   static constexpr int kTmemCols = (2 * TN < 32) ? 32 : 2 * TN;
   // stages | staging | scales | barriers: full[S], empty[S], acc_full[2],
-  // acc_empty[2], drain | tmem slot, flags
+  // acc_empty[2], drain, peer, done | tmem slot, flags
   static size_t bytes(int stages) {
     return 1024 /* alignment slack */ + static_cast<size_t>(stages) * kStageBytes +
-           kStagingBytes + kScalBytes + static_cast<size_t>(2 * stages + 5) * 8 + 64;
+           kStagingBytes + kScalBytes + static_cast<size_t>(2 * stages + 7) * 8 + 64;
   }
 };
 
@@ -373,8 +390,10 @@ __device__ __forceinline__ void emit_normal(const GemmArgs &a, const CUtensorMap
   }
 }
 
+// Decode tiles (TN <= 64) cap registers so two CTAs fit on an SM: with programmatic
+// dependent launch the next GEMM's CTA streams its weights beside this one.
 template <int TN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     w8a8_gemm_sm100(const __grid_constant__ CUtensorMap map_x,
                     const __grid_constant__ CUtensorMap map_y,
                     const __grid_constant__ CUtensorMap map_out,
@@ -393,7 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *acc_full = empty + S;
   uint64_t *acc_empty = acc_full + 2;
   uint64_t *drain = acc_empty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *peer_bar = drain + 1;  // cluster leader: contributors' partial sums have landed
+  uint64_t *done_bar = drain + 2;  // cluster contributor: the leader's ring is free for them
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 3);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile int *last_flag = abort_flag + 1;
 
@@ -410,6 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[i], kEpiWarps);
     }
     mbar_init(drain, 1);
+    mbar_init(peer_bar, 1);
+    mbar_init(done_bar, 1);
     *abort_flag = 0;
     *last_flag = 0;
     fence_barrier_init();
@@ -430,12 +453,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Every CTA's barriers are initialised before any CTA of the cluster signals them.
+  if (a.cluster > 1) cluster_sync();
+  // The next kernel in the stream may start its own prologue now; it waits for this
+  // grid before touching anything this grid writes.
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_x = a.swap ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_y = policy_evict_last();
+      // Weight tiles of the first stages are loaded before waiting for the previous
+      // kernel: inference weights are never written by the kernel just before.  The
+      // weight is X with swap_ab, else Y.  Activations wait for pdl_wait().
+      int pre = 0;
+      {
+        Schedule ps;
+        ps.init(a);
+        Segment sg;
+        while (pre < S && ps.next(a, sg)) {
+          int tx, ty;
+          tile_coords(a, sg.tile, tx, ty);
+          for (int kb = sg.kb0; kb < sg.kb1 && pre < S; ++kb, ++pre) {
+            mbar_arrive_expect_tx(&full[pre], L::kStageBytes);
+            if (a.swap)
+              tma_load_2d(sx + static_cast<size_t>(pre) * kXBytes, &map_x, &full[pre], kb * kBK,
+                          tx * kXRows, pol_x);
+            else
+              tma_load_2d(sy + static_cast<size_t>(pre) * L::kYBytes, &map_y, &full[pre],
+                          kb * kBK, ty * TN, pol_y);
+          }
+        }
+      }
+      pdl_wait();
       Schedule sch;
       sch.init(a);
       Segment seg;
@@ -447,16 +498,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         int tx, ty;
         tile_coords(a, seg.tile, tx, ty);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, a.status,
-                                 kStatusProducerWait)) {
-            ok = false;
-            break;
+          if (issued < pre) {
+            // Stage already claimed above with its weight tile: add the activation.
+            if (a.swap)
+              tma_load_2d(sy + static_cast<size_t>(stage) * L::kYBytes, &map_y, &full[stage],
+                          kb * kBK, ty * TN, pol_y);
+            else
+              tma_load_2d(sx + static_cast<size_t>(stage) * kXBytes, &map_x, &full[stage],
+                          kb * kBK, tx * kXRows, pol_x);
+          } else {
+            if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, a.status,
+                                   kStatusProducerWait)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+            tma_load_2d(sx + static_cast<size_t>(stage) * kXBytes, &map_x, &full[stage],
+                        kb * kBK, tx * kXRows, pol_x);
+            tma_load_2d(sy + static_cast<size_t>(stage) * L::kYBytes, &map_y, &full[stage],
+                        kb * kBK, ty * TN, pol_y);
           }
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(sx + static_cast<size_t>(stage) * kXBytes, &map_x, &full[stage],
-                      kb * kBK, tx * kXRows, pol_x);
-          tma_load_2d(sy + static_cast<size_t>(stage) * L::kYBytes, &map_y, &full[stage],
-                      kb * kBK, ty * TN, pol_y);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -535,6 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    pdl_wait();  // scales, outputs and the workspace belong to the stream's order
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const int epi_tid = threadIdx.x - 64;
@@ -587,7 +649,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!named_bar_and(2, kEpiWarps * 32, ok)) break;
       tc_fence_after();
       const bool whole = seg.kb0 == 0 && seg.kb1 == a.kblocks;
-      if (whole) {
+      if (a.cluster > 1) {
+        // Cluster split-K.  Once a CTA's MMAs are done its operand ring is idle.  The
+        // leader (rank 0) then arms its receive barrier and tells each contributor to
+        // go; contributors push their int32 partial sums into slot rank-1 of the
+        // leader's ring ([128 rows][TN] each) with st.async, which completes the
+        // barrier by bytes; the leader adds the slots to its own accumulator.
+        uint32_t *ring = reinterpret_cast<uint32_t *>(sx);
+        const uint32_t rank = cluster_ctarank();
+        const int nch = (t.ncols + 15) / 16;
+        if (rank != 0) {
+          const bool go = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(
+                                                      done_bar, 0, abort_flag, a.status,
+                                                      kStatusClusterWait));
+          const uint32_t bar0 = map_to_rank(smem_u32(peer_bar), 0);
+          const uint32_t slot0 = map_to_rank(
+              smem_u32(ring + (static_cast<size_t>(rank) - 1) * TN * kXRows + row * TN), 0);
+          for (int c = 0; c < nch; ++c) {
+            uint32_t r[16];
+            tmem_ld16(t.taddr + c * 16, r);
+            tmem_ld_wait();
+            if (go) {
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                st_async_v4(slot0 + (c * 16 + 4 * v) * 4,
+                            make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]), bar0);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        } else {
+          if (epi_tid == 0) {
+            mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * kXRows * 4));
+            for (int p = 1; p < a.cluster; ++p)
+              mbar_arrive_remote(map_to_rank(smem_u32(done_bar), static_cast<uint32_t>(p)));
+          }
+          const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(peer_bar, 0, abort_flag, a.status,
+                                                                      kStatusClusterWait));
+          for (int c0 = 0; c0 < t.ncols; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(t.taddr + c0, r);
+            tmem_ld_wait();
+            if (c0 + 16 >= t.ncols) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            if (!got) continue;
+            for (int p = 1; p < a.cluster; ++p) {
+              const uint4 *src = reinterpret_cast<const uint4 *>(
+                  ring + (static_cast<size_t>(p) - 1) * TN * kXRows + row * TN + c0);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const uint4 q = src[v];
+                r[4 * v] += q.x;
+                r[4 * v + 1] += q.y;
+                r[4 * v + 2] += q.z;
+                r[4 * v + 3] += q.w;
+              }
+            }
+            if (a.tma_out)
+              emit_swap16<TN>(a, &map_out, t, quarter, lane, c0, r, st);
+            else
+              epilogue_direct<TN>(a, t.tx, t.ty, row, c0, r);
+          }
+        }
+      } else if (whole) {
         if (!a.tma_out) {
           for (int c0 = 0; c0 < t.ncols; c0 += 16) {
             uint32_t r[16];
@@ -771,7 +899,10 @@ static int make_map(CUtensorMap *map, CUtensorMapDataType type, const void *ptr,
   return I8L_OK;
 }
 
-static size_t smem_extra() { return 1024 + kStagingBytes + kScalBytes + 5 * 8 + 64; }
+static size_t smem_extra() { return 1024 + kStagingBytes + kScalBytes + 7 * 8 + 64; }
+
+// Shared memory of one of two CTAs that share an SM (228 KB minus 1 KB reserved per CTA).
+constexpr int kHalfSmem = 233472 / 2 - 1024;
 
 static int max_stages_for(int tn, int smem_optin) {
   const int stage = kXBytes + tn * kBK;
@@ -789,7 +920,25 @@ struct Plan {
   long long sk_iters;
   int slots;
   size_t ws_bytes;
+  int cluster;  // CTAs per cluster splitting K of one tile (1 = none)
 };
+
+// Cluster size (1..8, at most the k-blocks) whose grid of tiles x size CTAs, one per
+// SM, keeps the most SMs streaming.  Ties go to the smaller cluster.
+static int best_cluster(int tiles, int kblocks, int sms) {
+  int best = 1;
+  double best_util = 0.0;
+  for (int cs = 1; cs <= 8 && cs <= kblocks; ++cs) {
+    const long long ctas = static_cast<long long>(tiles) * cs;
+    if (ctas > sms) break;
+    const double util = static_cast<double>(ctas) / sms;
+    if (util > best_util + 1e-9) {
+      best_util = util;
+      best = cs;
+    }
+  }
+  return best;
+}
 
 static void default_tile(int M, int N, int K, i8l_tile *t) {
   (void)N;
@@ -820,6 +969,7 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
       if (user->ctas) t.ctas = user->ctas;
       if (user->group) t.group = user->group;
       t.split = user->split;
+      t.cluster = user->cluster;
     }
   } else {
     t = *user;
@@ -837,7 +987,11 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
     p->tn = t.w_tile;
   }
   const int max_st = max_stages_for(p->tn, di.max_smem_optin);
-  if (t.stages <= 0) t.stages = max_st;
+  if (t.stages <= 0) {
+    t.stages = max_st;
+    // Decode tiles: leave room for a second CTA per SM (the next kernel under PDL).
+    if (t.swap_ab && p->tn <= 64) t.stages = std::max(2, std::min(max_st, max_stages_for(p->tn, kHalfSmem)));
+  }
   if (t.stages < 2 || t.stages > max_st)
     return set_error(I8L_ENOTSUP, "stages %d outside [2, %d] for this tile", t.stages, max_st);
   if (t.group <= 0) t.group = 1;
@@ -849,20 +1003,67 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   p->total_tiles = p->tiles_x * p->tiles_y;
   const long long total_iters = static_cast<long long>(p->total_tiles) * p->kblocks;
   int ctas = t.ctas > 0 ? t.ctas : di.sms;
-  if (t.split == 1) {
-    ctas = std::min(ctas, p->total_tiles);
+  int split = t.split;
+  p->cluster = 1;
+  if (split == 0) {
+    // Decode tiles with fewer tiles than SMs: split K inside thread-block clusters
+    // when that keeps most SMs streaming; many tiles: whole tiles unless the last
+    // wave would leave many SMs idle, then stream-K.
+    const int waves = (p->total_tiles + ctas - 1) / ctas;
+    const double wave_eff = static_cast<double>(p->total_tiles) / (static_cast<double>(waves) * ctas);
+    if (t.swap_ab && p->tn <= 64 && p->total_tiles < ctas) {
+      // Cluster split-K when it fills clearly more SMs than whole tiles, else whole tiles.
+      const int cs = best_cluster(p->total_tiles, p->kblocks, ctas);
+      split = (cs > 1 && p->total_tiles * cs >= p->total_tiles + ctas / 4) ? 3 : 1;
+    } else if (t.swap_ab && p->tn <= 64 && t.ctas <= 0 && p->total_tiles <= 2 * ctas) {
+      // Decode tiles fit two per SM: one CTA per tile, all resident at once.
+      split = 1;
+      ctas = p->total_tiles;
+    } else if (wave_eff >= 0.6 || p->total_tiles >= 4 * ctas) {
+      split = 1;  // the stream-K fix-up costs more than the idle share of the last wave
+    } else {
+      split = 2;
+    }
+  }
+  if (split == 3) {
+    if (!t.swap_ab || p->tn > 64)
+      return set_error(I8L_ENOTSUP, "cluster split-K takes swap_ab tiles of at most 64 tokens");
+    // The leader's operand ring receives (cluster-1) partial-sum slots of TN x 128 int32.
+    const long long ring = static_cast<long long>(t.stages) * (kXBytes + p->tn * kBK);
+    auto fits = [&](int c) { return static_cast<long long>(c - 1) * p->tn * kXRows * 4 <= ring; };
+    int cs = t.cluster;
+    if (cs <= 0) {
+      cs = best_cluster(p->total_tiles, p->kblocks, ctas);
+      while (cs > 1 && !fits(cs)) --cs;
+    }
+    if (cs < 1 || cs > 8 || cs > p->kblocks || !fits(cs))
+      return set_error(I8L_ENOTSUP,
+                       "cluster size %d outside [1, min(8, k-blocks=%d)] or its partial sums "
+                       "exceed the %lld-byte ring",
+                       cs, p->kblocks, ring);
+    if (cs == 1) split = 1;
+    p->cluster = cs;
+    ctas = p->total_tiles * cs;
     p->dp_tiles = p->total_tiles;
-  } else {
+  }
+  if (split == 1) {
+    if (p->cluster == 1) ctas = std::min(ctas, p->total_tiles);
+    p->dp_tiles = p->total_tiles;
+  } else if (split == 2) {
     if (static_cast<long long>(ctas) > total_iters) ctas = static_cast<int>(total_iters);
     const int waves = p->total_tiles / ctas;
     if (p->total_tiles % ctas == 0)
       p->dp_tiles = p->total_tiles;
     else
       p->dp_tiles = waves >= 1 ? (waves - 1) * ctas : 0;
+  } else if (split != 3) {
+    return set_error(I8L_ENOTSUP, "split mode %d unknown (0 auto, 1 whole, 2 stream-K, 3 cluster)", split);
   }
+  t.split = split;
+  t.cluster = p->cluster;
   t.ctas = ctas;
   p->ctas = ctas;
-  p->sk_iters = static_cast<long long>(p->total_tiles - p->dp_tiles) * p->kblocks;
+  p->sk_iters = p->cluster > 1 ? 0 : static_cast<long long>(p->total_tiles - p->dp_tiles) * p->kblocks;
   p->slots = p->sk_iters > 0 ? std::max(1, ctas - 1) : 0;
   const size_t counters_bytes = ((static_cast<size_t>(p->slots) * 4 + 255) / 256) * 256;
   p->ws_bytes = p->slots ? counters_bytes + static_cast<size_t>(p->slots) * kXRows * p->tn * 4 : 0;
@@ -887,7 +1088,9 @@ static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const CUtenso
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
-  w8a8_gemm_sm100<TN><<<ctas, kThreads, smem, stream>>>(mx, my, mo, mw, a);
+  e = launch(w8a8_gemm_sm100<TN>, dim3(ctas), dim3(kThreads), smem, stream, a.cluster, mx, my, mo,
+             mw, a);
+  if (e != cudaSuccess) return cuda_error(e, "gemm launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "gemm launch");
   return I8L_OK;
@@ -1006,6 +1209,7 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
       return e;
   }
   a.status = status_ptr();
+  a.cluster = p.cluster;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (p.tn) {
     case 16:

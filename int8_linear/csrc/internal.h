@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 #include <cuda_runtime.h>
 
 #include "../../include/int8_linear_b200.h"
@@ -27,5 +28,37 @@ int device_info(DeviceInfo *out);
 
 // Device pointer of the status word kernels set when a bounded wait gives up.
 int *status_ptr();
+
+// Whether kernels are launched with programmatic stream serialisation (PDL).
+bool pdl_enabled();
+
+// Launches `kernel` with the PDL attribute when pdl_enabled(), in thread-block
+// clusters of `cluster` CTAs along x when cluster > 1.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, int cluster, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace i8l

@@ -166,6 +166,8 @@ struct NormArgs {
 
 template <int DT, int NV, int VW>
 __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) add_rmsnorm_quant_kernel(const NormArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[32];
   using T = typename ActType<DT>::T;
   const long long row = blockIdx.x;
@@ -225,6 +227,8 @@ struct SiluArgs {
 
 template <int DT, int NV, int VW>
 __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) silu_mul_quant_kernel(const SiluArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[32];
   using T = typename ActType<DT>::T;
   const long long row = blockIdx.x;
@@ -265,6 +269,8 @@ struct QuantArgs {
 
 template <int DT, int NV, int VW>
 __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) quant_rows_kernel(const QuantArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[32];
   using T = typename ActType<DT>::T;
   const long long row = blockIdx.x;
@@ -334,7 +340,8 @@ int check_act(int act) {
   return I8L_OK;
 }
 
-int finish_launch(const char *what) {
+int finish_launch(cudaError_t err, const char *what) {
+  if (err != cudaSuccess) return cuda_error(err, what);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, what);
   return I8L_OK;
@@ -366,20 +373,21 @@ extern "C" int i8l_add_rmsnorm_quant(const void *x, int64_t ldx, const void *res
   if (!row_shape(K, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nv = rs.nv, th = rs.threads;
+  cudaError_t err = cudaSuccess;
   if (act_dtype == I8L_BF16) {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_BF16, NV, 8><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_BF16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
     } else {
-      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_BF16, NV, 1><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_BF16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   } else {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_F16, NV, 8><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_F16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
     } else {
-      I8L_DISPATCH_NV(nv, (add_rmsnorm_quant_kernel<I8L_F16, NV, 1><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_F16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   }
-  return finish_launch("add_rmsnorm_quant launch");
+  return finish_launch(err, "add_rmsnorm_quant launch");
 }
 
 extern "C" int i8l_silu_mul_quant(const void *gate_up, int64_t ld, int32_t act_dtype, int8_t *q,
@@ -397,20 +405,21 @@ extern "C" int i8l_silu_mul_quant(const void *gate_up, int64_t ld, int32_t act_d
   if (!row_shape(I, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nv = rs.nv, th = rs.threads;
+  cudaError_t err = cudaSuccess;
   if (act_dtype == I8L_BF16) {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_BF16, NV, 8><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(silu_mul_quant_kernel<I8L_BF16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
     } else {
-      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_BF16, NV, 1><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(silu_mul_quant_kernel<I8L_BF16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   } else {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_F16, NV, 8><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(silu_mul_quant_kernel<I8L_F16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
     } else {
-      I8L_DISPATCH_NV(nv, (silu_mul_quant_kernel<I8L_F16, NV, 1><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(silu_mul_quant_kernel<I8L_F16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   }
-  return finish_launch("silu_mul_quant launch");
+  return finish_launch(err, "silu_mul_quant launch");
 }
 
 extern "C" int i8l_quant_rows(const void *x, int64_t ldx, int32_t act_dtype, int8_t *q,
@@ -428,18 +437,19 @@ extern "C" int i8l_quant_rows(const void *x, int64_t ldx, int32_t act_dtype, int
   if (!row_shape(K, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nv = rs.nv, th = rs.threads;
+  cudaError_t err = cudaSuccess;
   if (act_dtype == I8L_BF16) {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_BF16, NV, 8><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(quant_rows_kernel<I8L_BF16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
     } else {
-      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_BF16, NV, 1><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(quant_rows_kernel<I8L_BF16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   } else {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_F16, NV, 8><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(quant_rows_kernel<I8L_F16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
     } else {
-      I8L_DISPATCH_NV(nv, (quant_rows_kernel<I8L_F16, NV, 1><<<M, th, 0, s>>>(a)))
+      I8L_DISPATCH_NV(nv, (err = launch(quant_rows_kernel<I8L_F16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   }
-  return finish_launch("quant_rows launch");
+  return finish_launch(err, "quant_rows launch");
 }

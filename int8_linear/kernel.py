@@ -51,8 +51,13 @@ class Config:
     stages  shared-memory ring depth, 0 for the most that fits.
     group_m 128-row tiles walked together so concurrent CTAs share tiles in L2.
     swap_ab None picks swap_ab for bm != 128.
-    split   0: stream-K over the SMs with an exact int32 fix-up; 1: whole tiles only.
+    split   how K is shared out; int32 partial sums are always reduced exactly, so every
+            choice gives the same bits: 0 the library's choice, 1 whole tiles, 2
+            stream-K over the SMs (reduced in a workspace), 3 cluster split-K (the CTAs
+            of a thread-block cluster split a tile's K and reduce over distributed
+            shared memory; swap_ab tiles of at most 64 tokens).
     ctas    persistent CTAs, 0 for one per SM.
+    cluster CTAs per cluster for split=3, 0 for the library's choice.
     """
 
     bm: int
@@ -64,6 +69,7 @@ class Config:
     swap_ab: bool | None = None
     split: int = 0
     ctas: int = 0
+    cluster: int = 0
 
     @property
     def swapped(self) -> bool:
@@ -71,7 +77,9 @@ class Config:
 
     @property
     def name(self) -> str:
-        tail = (" swap" if self.swapped else "") + (" whole" if self.split == 1 else "")
+        tail = (" swap" if self.swapped else "") + {0: "", 1: " whole", 2: " sk", 3: " cl"}.get(
+            self.split, f" split{self.split}")
+        tail += str(self.cluster) if self.split == 3 and self.cluster else ""
         tail += f" c{self.ctas}" if self.ctas else ""
         return f"{self.bm}x{self.bn}x{self.bk} w{self.warps} s{self.stages} g{self.group_m}{tail}"
 
@@ -84,24 +92,33 @@ class Config:
                 raise NotSupported(f"{self.name}: swap_ab tiles are bm in {TOKEN_TILES} x bn 128")
         elif self.bm != 128 or self.bn not in (128, 256):
             raise NotSupported(f"{self.name}: tiles are bm 128 x bn in (128, 256)")
-        if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1):
+        if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1, 2, 3):
             raise NotSupported(f"{self.name}: bad stages/group_m/split")
+        if self.split == 3 and (not self.swapped or self.bm > 64 or not 0 <= self.cluster <= 8):
+            raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles of <= 64 tokens")
 
     def as_tile(self) -> _native.I8LTile:
         return _native.I8LTile(
             swap_ab=1 if self.swapped else 0, tok_tile=self.bm if self.swapped else 128,
             w_tile=128 if self.swapped else self.bn, stages=self.stages, ctas=self.ctas,
-            group=self.group_m, split=self.split, reserved=0)
+            group=self.group_m, split=self.split, cluster=self.cluster)
 
 
 def default_config(m: int, n: int, k: int) -> Config:
     """The untuned choice.  Decode batches (M <= 256) put the weight on the 128-row
     MMA side and the tokens on the narrow side, the smallest token tile that holds
-    M; larger batches use 128 x 256 tiles.  Both split K across the SMs (stream-K)
-    whenever whole tiles would leave SMs idle."""
+    M; larger batches use 128 x 256 tiles.  The library then splits K when whole
+    tiles would leave SMs idle: inside thread-block clusters for decode tiles, by
+    stream-K otherwise."""
     if m <= 256:
         return Config(next(t for t in TOKEN_TILES if t >= m), 128)
-    return Config(128, 256)
+    # Prefill: the wider tile unless the narrower one fills the SMs clearly better.
+    sms = 148
+    def waves_eff(bn):
+        tiles = -(-m // 128) * -(-n // bn)
+        waves = -(-tiles // sms)
+        return tiles / (waves * sms)
+    return Config(128, 256) if waves_eff(256) >= 0.8 * waves_eff(128) else Config(128, 128)
 
 
 @lru_cache(maxsize=None)

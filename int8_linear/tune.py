@@ -1,0 +1,165 @@
+"""Per-shape tile tuner for B200: writes int8_linear/tuned_configs.json.
+
+    python -m int8_linear.tune [--shapes qwen3-1.7b-vllm llama-3-8b] [--m 1 2 4 ...]
+                               [--tp 1 2 4 8] [--out PATH]
+
+Same table format as the reference's tuned_configs.json (read by tuned_config,
+int8_linear/kernel.py):  {device name: {"KxN": {"M": {"config": {...}, "graph_us": t}}}}.
+For every (K, N, M) each candidate tiling is timed as a CUDA graph of back-to-back
+launches, each on its own copy of the weight (L2-cold, as in a decode step that streams
+every layer's weights), with programmatic dependent launch on; the fastest goes into
+the table.  A candidate whose int32 product differs from the default tiling's is
+rejected (all tilings must give identical bits).  --tp N also tunes the per-GPU shards
+of a tensor-parallel split (column shards N/g of qkv and gate_up, row shards K/g of
+o_proj and down).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+from dataclasses import asdict
+
+import torch
+
+from int8_linear import _native
+from int8_linear.kernel import TOKEN_TILES, TUNED_PATH, Config, NotSupported, default_config, w8a8_mm
+from int8_linear.shapes import SHAPES
+
+M_DEFAULT = [1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 1024, 4096]
+COPIES = 8
+
+
+def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
+    """Tilings worth timing for this shape (deduplicated, each B200-valid)."""
+    out: list[Config] = [default_config(m, n, k)]
+    cdiv = lambda a, b: -(-a // b)  # noqa: E731
+    if m <= 256:
+        holding = [t for t in TOKEN_TILES if t >= m][:1]
+        smaller = [t for t in TOKEN_TILES if t < m and t >= m / 4][-1:]
+        for tn in holding + smaller:
+            tiles = cdiv(n, 128) * cdiv(m, tn)
+            out += [Config(tn, 128, split=1), Config(tn, 128, split=1, ctas=tiles),
+                    Config(tn, 128, split=2)]
+            if tn <= 64:
+                out += [Config(tn, 128, split=3)] + [Config(tn, 128, split=3, cluster=c) for c in (2, 4, 8)]
+    if m >= 64:
+        for bn in (128, 256):
+            out += [Config(128, bn, split=1), Config(128, bn, split=2)]
+    seen, uniq = set(), []
+    for c in out:
+        if c.name in seen:
+            continue
+        try:
+            c.check()
+        except NotSupported:
+            continue
+        seen.add(c.name)
+        uniq.append(c)
+    return uniq
+
+
+def graph_us(fn, reps: int, windows: int = 5) -> float:
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(windows):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3 / reps)
+    del graph
+    return statistics.median(times)
+
+
+def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True) -> dict:
+    g = torch.Generator(device="cuda").manual_seed(k * 31 + n)
+    ws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+          for _ in range(COPIES)]
+    sb = torch.rand((n, 1), device="cuda", generator=g) * 1e-3 + 1e-4
+    one = torch.ones(1, device="cuda")
+    table = {}
+    for m in ms:
+        a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+        sa = torch.rand((m, 1), device="cuda", generator=g) * 1e-2 + 1e-3
+        want = w8a8_mm(a, ws[0].t(), one, one, raw=True, config=default_config(m, n, k))
+        best = None
+        for cfg in candidates(m, n, k, sms):
+            try:
+                got = w8a8_mm(a, ws[0].t(), one, one, raw=True, config=cfg)
+            except NotSupported:
+                continue
+            if not torch.equal(got, want):
+                raise AssertionError(f"{cfg.name} differs from the default tiling at {m}x{k}x{n}")
+            it = iter(range(1 << 40))
+
+            def fn(cfg=cfg, it=it):
+                w8a8_mm(a, ws[next(it) % COPIES].t(), sa, sb, torch.bfloat16, config=cfg)
+
+            us = graph_us(fn, COPIES)
+            if best is None or us < best[1]:
+                best = (cfg, us)
+        assert best is not None
+        cfg, us = best
+        table[str(m)] = {"config": asdict(cfg), "graph_us": round(us, 3)}
+        if verbose:
+            print(f"K={k:6d} N={n:6d} M={m:5d}: {cfg.name:40s} {us:9.2f} us", flush=True)
+    del ws
+    torch.cuda.empty_cache()
+    return table
+
+
+def shard_shapes(model: str, tp: int) -> list[tuple[int, int]]:
+    """(K, N) per GPU: column shards for qkv and gate_up, row shards for o_proj and down."""
+    out = []
+    for label, k, n in SHAPES[model]:
+        row_parallel = label.startswith(("o_proj", "down"))
+        out.append((k // tp, n) if row_parallel else (k, n // tp))
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shapes", nargs="*", default=["qwen3-1.7b-vllm", "llama-3-8b"])
+    ap.add_argument("--m", nargs="*", type=int, default=M_DEFAULT)
+    ap.add_argument("--tp", nargs="*", type=int, default=[1])
+    ap.add_argument("--out", default=str(TUNED_PATH))
+    args = ap.parse_args()
+    _native.set_pdl(True)
+    dev = torch.cuda.get_device_name()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    try:
+        with open(args.out) as f:
+            tables = json.load(f)
+    except FileNotFoundError:
+        tables = {}
+    table = tables.setdefault(dev, {})
+    done = set()
+    for model in args.shapes:
+        for tp in args.tp:
+            for k, n in shard_shapes(model, tp):
+                if (k, n) in done:
+                    continue
+                done.add((k, n))
+                table.setdefault(f"{k}x{n}", {}).update(tune_shape(k, n, args.m, sms))
+                with open(args.out, "w") as f:
+                    json.dump(tables, f, indent=1, sort_keys=True)
+                    f.write("\n")
+    print("wrote", args.out)
+
+
+if __name__ == "__main__":
+    main()

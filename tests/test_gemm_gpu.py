@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from int8_linear import Config, NotSupported, _native, w8a8_mm
-from int8_linear.kernel import choose_config
+from int8_linear.kernel import choose_config, default_config
 from oracle import gemm as og
 from oracle.numerics import to_bits
 from tests.gpu_util import bits, ints, np_, offset_ints
@@ -39,9 +39,14 @@ def test_int32_product_is_exact(m, k, n):
 
 
 TILINGS = [Config(t, 128) for t in (16, 32, 64, 128, 256)] + [
+    Config(t, 128, split=2) for t in (16, 32, 64, 128, 256)] + [
     Config(128, 128, swap_ab=True), Config(128, 128), Config(128, 256),
-    Config(16, 128, split=1), Config(128, 256, split=1), Config(64, 128, stages=2),
-    Config(128, 256, stages=2, group_m=1), Config(32, 128, ctas=7), Config(128, 128, ctas=3),
+    Config(16, 128, split=1), Config(128, 256, split=1), Config(128, 256, split=2),
+    Config(64, 128, stages=2), Config(128, 256, stages=2, group_m=1),
+    Config(32, 128, ctas=7, split=2), Config(128, 128, ctas=3, split=2),
+    Config(16, 128, split=3), Config(32, 128, split=3, cluster=2), Config(64, 128, split=3, cluster=2),
+    Config(16, 128, split=3, cluster=3), Config(16, 128, split=3, cluster=8),
+    Config(16, 128, split=3, cluster=1), Config(64, 128, split=1, ctas=1000),
 ]
 
 
@@ -102,6 +107,12 @@ def test_decode_and_prefill_bf16_bit_exact(m, k, n):
     assert np.array_equal(bits(got), want)
 
 
+def test_declines_a_cluster_whose_partial_sums_do_not_fit():
+    a, w = ints((64, 2048), 1), ints((1024, 2048), 2)
+    with pytest.raises(NotSupported, match="ring"):
+        w8a8_mm(a, w.t(), one(), one(), config=Config(64, 128, split=3, cluster=8))
+
+
 def test_declines_shapes_the_kernel_does_not_take():
     a, w = ints((4, 100), 8), ints((64, 100), 9)
     with pytest.raises(NotSupported):
@@ -141,14 +152,33 @@ def test_exact_on_an_odd_pointer_repeatedly():
         assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True)), exact(a, w))
 
 
-def test_repeated_split_calls_leave_the_workspace_clean():
-    """Stream-K tiles reduce through the workspace and zero it again; many calls with
-    different shapes in a row must each stay exact."""
+@pytest.mark.parametrize("split", [0, 2, 3])
+def test_repeated_split_calls_leave_the_workspace_clean(split):
+    """Split tiles reduce through the workspace (stream-K) or distributed shared memory
+    (cluster) and leave nothing behind; many calls with different shapes in a row must
+    each stay exact."""
     for i, (m, k, n) in enumerate([(1, 2048, 2048), (3, 6144, 2048), (16, 2048, 12288),
-                                   (1, 14336, 4096), (256, 2048, 2048), (1, 2048, 2048)] * 2):
+                                   (1, 14336, 4096), (40, 2048, 2048), (1, 2048, 2048)] * 2):
         a, w = ints((m, k), 30 + i), ints((n, k), 40 + i)
-        assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True)), exact(a, w))
+        cfg = default_config(m, n, k)
+        cfg = Config(cfg.bm, cfg.bn, split=split)
+        assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), exact(a, w))
     assert _native.read_status() == 0
+
+
+@pytest.mark.parametrize("m", [1, 5, 16, 40, 64])
+@pytest.mark.parametrize("k,n", [(2048, 4096), (2048, 2048), (6144, 2048), (2048, 12288), (14336, 4096)])
+def test_cluster_split_bf16_bit_exact(m, k, n):
+    """Decode shapes through cluster split-K, bf16 out with bias."""
+    a, w = ints((m, k), 80 + m), ints((n, k), 81)
+    g = torch.Generator().manual_seed(82)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    cfg = default_config(m, n, k)
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=Config(cfg.bm, cfg.bn, split=3))
+    want = to_bits(og.epilogue_f32(exact(a, w), np_(sa), np_(sb), np_(bias)), "bf16")
+    assert np.array_equal(bits(got), want)
 
 
 @pytest.mark.parametrize("m,n", [(1, 1040), (37, 1000), (300, 1040), (513, 2056), (200, 136)])

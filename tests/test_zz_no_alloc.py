@@ -33,9 +33,9 @@ def _args(a, w, sa, sb, bias, out):
             a.shape[0], w.shape[0], a.shape[1])
 
 
-# Stream-K tiles (split=0): their split tiles reduce through the scratch.
-CASES = [(1, 2048, 4096, Config(16, 128)), (16, 6144, 2048, Config(16, 128)),
-         (33, 2048, 12288, Config(64, 128))]
+# Stream-K tiles (split=2): their split tiles reduce through the scratch.
+CASES = [(1, 2048, 4096, Config(16, 128, split=2)), (16, 6144, 2048, Config(16, 128, split=2)),
+         (33, 2048, 12288, Config(64, 128, split=2))]
 
 
 @pytest.mark.parametrize("m,k,n,cfg", CASES, ids=lambda v: getattr(v, "name", v))
@@ -74,7 +74,7 @@ def test_noalloc_rejects_problems_whose_scratch_does_not_fit():
     a, w = ints((m, k), 1), ints((n, k), 2)
     one = torch.ones(1, device="cuda")
     out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
-    tile = Config(128, 256).as_tile()
+    tile = Config(128, 256, split=2).as_tile()
     need = lib.i8l_workspace_size(m, n, k, ctypes.byref(tile))
     assert need > 8 << 20
     rc = lib.i8l_w8a8_mm_noalloc(a.data_ptr(), k, w.data_ptr(), k, one.data_ptr(), 0,
