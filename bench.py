@@ -49,9 +49,10 @@ L2_BYTES = 126 << 20
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-triton", "reference-triton-child"],
+                    default="ours")
     ap.add_argument("--model", default="qwen3-1.7b-vllm")
     ap.add_argument("--no-standin", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -101,7 +102,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -351,15 +352,17 @@ def run_ours(args, world, rank, dev):
         e2e = run_e2e(layers, acts, cases, dev, world, max(1, min(args.steps, 5)))
 
     del graphs
-    standin = None
+    standin = quant = None
     if not args.no_standin and world == 1:
         standin = run_standin(dev)
+        quant = run_quantisers(dev)
 
     launches = args.steps * len(cases) * COPIES
     return {
         "value": round(value_us, 2), "ms_per_step": round(ms, 4), "per_shape": per_shape,
         "l2_warm_us": warm, "roofline": roofline, "roofline_other": other,
         "allgather_us_per_sweep": allgather_us, "e2e": e2e, "standin_us_per_layer": standin,
+        "quantisers": quant,
         "clocks": clocks.summary(), "gpu_launches": launches,
     }
 
@@ -411,6 +414,32 @@ def run_e2e(layers, acts, cases, dev, world, passes):
     return {"value": round(us, 2), "unit": "us", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "passes": passes,
             "note": "one eager pass over the sweep through int8_linear.w8a8_mm, host copies included"}
+
+
+def run_quantisers(dev):
+    """the fused quantisers, µs per call (graph of 50 calls) and the
+    fraction of HBM bandwidth their algorithmic bytes reach."""
+    import torch
+
+    from int8_linear import fused_quant as fq
+
+    pk = peaks()
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(3)
+    gamma = (1.0 + 0.1 * torch.randn(2048, generator=g, device=dev)).to(torch.bfloat16)
+    for m in (1, 16, 64, 128, 1024, 4096):
+        x = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
+        r = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
+        gu = torch.randn((m, 12288), generator=g, device=dev).to(torch.bfloat16)
+        t_norm = time_graph(capture(lambda: [fq.add_rmsnorm_quant(x, r, gamma, 1e-6) for _ in range(50)])) / 50
+        t_silu = time_graph(capture(lambda: [fq.silu_mul_quant(gu, True, True) for _ in range(50)])) / 50
+        b_norm = m * (2048 * 7 + 4) + 2 * 2048
+        b_silu = m * (6144 * 5 + 4)
+        out[str(m)] = {"add_rmsnorm_quant_us": round(t_norm, 2),
+                       "add_rmsnorm_quant_hbm_frac": round(b_norm / t_norm / 1e3 / pk["hbm_gbs"], 3),
+                       "silu_mul_quant_us": round(t_silu, 2),
+                       "silu_mul_quant_hbm_frac": round(b_silu / t_silu / 1e3 / pk["hbm_gbs"], 3)}
+    return out
 
 
 def run_standin(dev):
@@ -485,9 +514,116 @@ def run_reference(args, world, rank):
     }
 
 
+# ------------------------------------------------------------------- reference Triton arm
+REF_INSTALL = ROOT / "baseline" / "_ref"
+
+
+def run_reference_triton_child(args):
+    """In a process whose only int8_linear is the installed reference (baseline/_ref):
+    its Triton w8a8_mm over the same sweep (L2-cold, same timing) and its stand-in
+    (bench/fuse_quant.py Stack.fused structure, vLLM's scaled_int8_quant where the
+    reference uses it, else the same per-token quantiser in torch)."""
+    import torch
+
+    import int8_linear as ref
+    from int8_linear import fused_quant as rfq
+    from int8_linear.kernel import w8a8_mm as ref_mm
+
+    assert str(REF_INSTALL) in ref.__file__, ref.__file__
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    per = {}
+    for name, k, n in layers_for(args.model):
+        ws = [quant_rows_t((torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16))
+              for _ in range(COPIES)]
+        for m in M_SWEEP:
+            a_q, a_s = quant_rows_t(torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16))
+            it = iter(range(1 << 40))
+
+            def fn():
+                for _ in range(COPIES):
+                    wq, wsc = ws[next(it) % COPIES]
+                    ref_mm(a_q, wq.t(), a_s, wsc, torch.bfloat16)
+            per[f"{name}/{m}"] = round(time_graph(capture(fn)) / COPIES, 3)
+        del ws
+    total = sum(per.values())
+    try:
+        from vllm import _custom_ops as ops
+
+        def q8(x):
+            q, s_, _ = ops.scaled_int8_quant(x)
+            return q, s_
+        q8(torch.randn((2, 2048), device=dev).to(torch.bfloat16))
+        qsrc = "vllm scaled_int8_quant"
+    except Exception as e:  # noqa: BLE001
+        qsrc = f"torch per-token quantiser ({type(e).__name__} loading vLLM ops)"
+
+        def q8(x):
+            xf = x.float()
+            am = xf.abs().amax(-1, keepdim=True)
+            inv = torch.where(am == 0, torch.zeros_like(am), 127.0 / am)
+            return torch.round(xf * inv).clamp(-128, 127).to(torch.int8), am / 127.0
+    standin = {}
+    from int8_linear.shapes import SHAPES as RS  # noqa: F401  (the reference's own table)
+    for m in STANDIN_BATCHES:
+        gg = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn((m, 2048), generator=gg, device=dev).to(torch.bfloat16)
+        w = torch.ones(2048, device=dev, dtype=torch.bfloat16)
+        layers = []
+        for _ in range(28):
+            layer = {}
+            for nm, (k, n) in {"qkv": (2048, 4096), "o": (2048, 2048), "gu": (2048, 12288),
+                               "dn": (6144, 2048)}.items():
+                wq = torch.randint(-127, 128, (n, k), generator=gg, device=dev, dtype=torch.int8)
+                layer[nm] = (wq.t(), torch.rand((n, 1), generator=gg, device=dev) * 1e-3 + 1e-4)
+            layers.append(layer)
+
+        def step():
+            res = x
+            q, s_, _ = rfq.add_rmsnorm_quant(x, None, w, 1e-6, True)
+            h = None
+            for i, L in enumerate(layers):
+                if i:
+                    q, s_, res = rfq.add_rmsnorm_quant(h, res, w, 1e-6, True)
+                a = ref_mm(q, L["qkv"][0], s_, L["qkv"][1], torch.bfloat16)[:, :2048].contiguous()
+                q, s_ = q8(a)
+                h = ref_mm(q, L["o"][0], s_, L["o"][1], torch.bfloat16)
+                q, s_, res = rfq.add_rmsnorm_quant(h, res, w, 1e-6, True)
+                gu = ref_mm(q, L["gu"][0], s_, L["gu"][1], torch.bfloat16)
+                q, s_ = rfq.silu_mul_quant(gu, True, True)
+                h = ref_mm(q, L["dn"][0], s_, L["dn"][1], torch.bfloat16)
+            return h
+        standin[str(m)] = round(statistics.median([time_graph(capture(step)) for _ in range(3)]) / 28, 2)
+        del layers
+        torch.cuda.empty_cache()
+    print(json.dumps({"value": round(total, 2), "per_shape_us": per, "standin_us_per_layer": standin,
+                      "standin_o_proj_quantiser": qsrc, "triton": __import__("triton").__version__}))
+
+
+def run_reference_triton(args, rank):
+    """The reference's own Triton kernels on this GPU (not the CPU reference arm):
+    a child process with PYTHONPATH set to the installed reference."""
+    if rank != 0:
+        return None
+    if not (REF_INSTALL / "int8_linear").exists():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    env = dict(os.environ, PYTHONPATH=str(REF_INSTALL))
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference-triton-child",
+           "--model", args.model]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=1800)
+    if r.returncode != 0:
+        return {"unavailable": "reference Triton run failed: " + (r.stderr.strip().splitlines() or ["?"])[-1]}
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
 # ------------------------------------------------------------------- main
 def main():
     args = parse()
+    if args.impl == "reference-triton-child":
+        # Only the installed reference may provide int8_linear in this process.
+        sys.path[:] = [str(REF_INSTALL)] + [p for p in sys.path if Path(p or ".").resolve() != ROOT]
+        run_reference_triton_child(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -501,6 +637,11 @@ def main():
                        "l2": f"cold: {COPIES} weight copies per layer rotated, inputs > L2",
                        "parallelism": f"column-parallel N/{world}" if world > 1 else "single GPU",
                        "pdl": not args.no_pdl}}
+    if args.impl == "reference-triton":
+        res = run_reference_triton(args, rank)
+        if rank == 0:
+            print(json.dumps(dict(base, impl="reference-triton", dtype="i8", **res)), flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, world, rank)
         if rank == 0:

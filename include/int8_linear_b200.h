@@ -55,7 +55,9 @@ extern "C" {
  *                the CTAs of a thread-block cluster split one tile's K and reduce over
  *                distributed shared memory (swap_ab tiles of up to 64 tokens; no
  *                workspace);
- *   cluster:     CTAs per cluster for split = 3 (0 = the library's choice, <= 8).
+ *   cluster:     CTAs per cluster for split = 3 (0 = the library's choice, <= 8);
+ *   store:       output path: 0 = the library's choice, 1 = TMA stores through
+ *                shared memory, 2 = plain stores.
  */
 typedef struct i8l_tile {
   int32_t swap_ab;
@@ -66,6 +68,7 @@ typedef struct i8l_tile {
   int32_t group;
   int32_t split;
   int32_t cluster;
+  int32_t store;
 } i8l_tile;
 
 /*

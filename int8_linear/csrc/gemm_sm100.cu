@@ -65,6 +65,7 @@ struct GemmArgs {
   int *counters;  // one k-block counter per slot
   int *status;
   int cluster;    // >1: the CTAs of each cluster split K of one tile (reduced over DSMEM)
+  int cluster_early;  // contributors push into the leader's staging area without waiting
 };
 
 struct Segment {
@@ -433,6 +434,14 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     mbar_init(drain, 1);
     mbar_init(peer_bar, 1);
     mbar_init(done_bar, 1);
+    if (a.cluster_early && cluster_ctarank() == 0) {
+      // One tile per cluster: its partial sums arrive as (cluster-1) slots of the
+      // live column chunks.  Armed before the cluster sync, so before any byte lands.
+      int tx, ty;
+      tile_coords(a, static_cast<int>(blockIdx.x) / a.cluster, tx, ty);
+      const int nch = (live_cols<TN>(a, ty) + 15) / 16;
+      mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * kXRows * 4));
+    }
     *abort_flag = 0;
     *last_flag = 0;
     fence_barrier_init();
@@ -655,11 +664,14 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
         // go; contributors push their int32 partial sums into slot rank-1 of the
         // leader's ring ([128 rows][TN] each) with st.async, which completes the
         // barrier by bytes; the leader adds the slots to its own accumulator.
-        uint32_t *ring = reinterpret_cast<uint32_t *>(sx);
+        // Early mode: the slots are the leader's staging area, free from the start (the
+        // leader then stores directly), so contributors push as soon as they are done.
+        uint32_t *ring = reinterpret_cast<uint32_t *>(a.cluster_early ? staging : sx);
         const uint32_t rank = cluster_ctarank();
         const int nch = (t.ncols + 15) / 16;
         if (rank != 0) {
-          const bool go = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(
+          const bool go = a.cluster_early ||
+                          __all_sync(0xffffffffu, mbar_wait_cluster_bounded(
                                                       done_bar, 0, abort_flag, a.status,
                                                       kStatusClusterWait));
           const uint32_t bar0 = map_to_rank(smem_u32(peer_bar), 0);
@@ -680,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
         } else {
-          if (epi_tid == 0) {
+          if (epi_tid == 0 && !a.cluster_early) {
             mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * kXRows * 4));
             for (int p = 1; p < a.cluster; ++p)
               mbar_arrive_remote(map_to_rank(smem_u32(done_bar), static_cast<uint32_t>(p)));
@@ -1183,8 +1195,11 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   const int esize = (out_dtype == I8L_BF16 || out_dtype == I8L_F16) ? 2 : 4;
   const bool aligned_out = reinterpret_cast<uintptr_t>(out) % 16 == 0 && (ldc * esize) % 16 == 0;
   a.vec_store = aligned_out ? 1 : 0;
+  // Output path: TMA stores through shared memory, or plain stores (cheaper for the
+  // few rows of a decode batch).  store: 0 auto, 1 TMA, 2 direct.
+  const int store = tile && tile->store ? tile->store : ((swap && M <= 32) ? 2 : 1);
   CUtensorMap mo{}, mw{};
-  if (aligned_out) {
+  if (aligned_out && store == 1) {
     static const CUtensorMapDataType kTypes[4] = {
         CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
         CU_TENSOR_MAP_DATA_TYPE_FLOAT32, CU_TENSOR_MAP_DATA_TYPE_INT32};
@@ -1210,6 +1225,10 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   }
   a.status = status_ptr();
   a.cluster = p.cluster;
+  // Early cluster mode needs the (cluster-1) slots, each TN x 128 int32 apart, inside
+  // the leader's staging area, which plain stores leave unused.
+  if (p.cluster > 1 && !a.tma_out)
+    a.cluster_early = static_cast<long long>(p.cluster - 1) * p.tn * kXRows * 4 <= kStagingBytes ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (p.tn) {
     case 16:

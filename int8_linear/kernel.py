@@ -58,6 +58,7 @@ class Config:
             shared memory; swap_ab tiles of at most 64 tokens).
     ctas    persistent CTAs, 0 for one per SM.
     cluster CTAs per cluster for split=3, 0 for the library's choice.
+    store   output path: 0 the library's choice, 1 TMA stores, 2 plain stores.
     """
 
     bm: int
@@ -70,6 +71,7 @@ class Config:
     split: int = 0
     ctas: int = 0
     cluster: int = 0
+    store: int = 0
 
     @property
     def swapped(self) -> bool:
@@ -81,6 +83,7 @@ class Config:
             self.split, f" split{self.split}")
         tail += str(self.cluster) if self.split == 3 and self.cluster else ""
         tail += f" c{self.ctas}" if self.ctas else ""
+        tail += {1: " tma", 2: " direct"}.get(self.store, "")
         return f"{self.bm}x{self.bn}x{self.bk} w{self.warps} s{self.stages} g{self.group_m}{tail}"
 
     def check(self) -> None:
@@ -94,6 +97,8 @@ class Config:
             raise NotSupported(f"{self.name}: tiles are bm 128 x bn in (128, 256)")
         if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1, 2, 3):
             raise NotSupported(f"{self.name}: bad stages/group_m/split")
+        if self.store not in (0, 1, 2):
+            raise NotSupported(f"{self.name}: store must be 0, 1 or 2")
         if self.split == 3 and (not self.swapped or self.bm > 64 or not 0 <= self.cluster <= 8):
             raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles of <= 64 tokens")
 
@@ -101,7 +106,7 @@ class Config:
         return _native.I8LTile(
             swap_ab=1 if self.swapped else 0, tok_tile=self.bm if self.swapped else 128,
             w_tile=128 if self.swapped else self.bn, stages=self.stages, ctas=self.ctas,
-            group=self.group_m, split=self.split, cluster=self.cluster)
+            group=self.group_m, split=self.split, cluster=self.cluster, store=self.store)
 
 
 def default_config(m: int, n: int, k: int) -> Config:

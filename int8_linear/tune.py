@@ -43,7 +43,10 @@ def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
             out += [Config(tn, 128, split=1), Config(tn, 128, split=1, ctas=tiles),
                     Config(tn, 128, split=2)]
             if tn <= 64:
-                out += [Config(tn, 128, split=3)] + [Config(tn, 128, split=3, cluster=c) for c in (2, 4, 8)]
+                out += [Config(tn, 128, split=3)] + [Config(tn, 128, split=3, cluster=c) for c in (2, 3, 4, 8)]
+            if m <= 32:   # plain versus TMA stores for the few output rows
+                out += [Config(tn, 128, split=3, cluster=c, store=1) for c in (2, 4)]
+                out += [Config(tn, 128, split=1, store=1), Config(tn, 128, split=2, store=2)]
     if m >= 64:
         for bn in (128, 256):
             out += [Config(128, bn, split=1), Config(128, bn, split=2)]

@@ -47,6 +47,9 @@ TILINGS = [Config(t, 128) for t in (16, 32, 64, 128, 256)] + [
     Config(16, 128, split=3), Config(32, 128, split=3, cluster=2), Config(64, 128, split=3, cluster=2),
     Config(16, 128, split=3, cluster=3), Config(16, 128, split=3, cluster=8),
     Config(16, 128, split=3, cluster=1), Config(64, 128, split=1, ctas=1000),
+    Config(16, 128, split=3, cluster=2, store=2), Config(16, 128, split=3, cluster=3, store=2),
+    Config(32, 128, split=3, cluster=2, store=2), Config(16, 128, split=3, cluster=4, store=1),
+    Config(16, 128, split=2, store=2), Config(256, 128, store=2), Config(128, 256, store=2),
 ]
 
 
@@ -166,9 +169,10 @@ def test_repeated_split_calls_leave_the_workspace_clean(split):
     assert _native.read_status() == 0
 
 
+@pytest.mark.parametrize("store", [0, 1, 2])
 @pytest.mark.parametrize("m", [1, 5, 16, 40, 64])
 @pytest.mark.parametrize("k,n", [(2048, 4096), (2048, 2048), (6144, 2048), (2048, 12288), (14336, 4096)])
-def test_cluster_split_bf16_bit_exact(m, k, n):
+def test_cluster_split_bf16_bit_exact(m, k, n, store):
     """Decode shapes through cluster split-K, bf16 out with bias."""
     a, w = ints((m, k), 80 + m), ints((n, k), 81)
     g = torch.Generator().manual_seed(82)
@@ -176,7 +180,7 @@ def test_cluster_split_bf16_bit_exact(m, k, n):
     sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
     cfg = default_config(m, n, k)
-    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=Config(cfg.bm, cfg.bn, split=3))
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=Config(cfg.bm, cfg.bn, split=3, store=store))
     want = to_bits(og.epilogue_f32(exact(a, w), np_(sa), np_(sb), np_(bias)), "bf16")
     assert np.array_equal(bits(got), want)
 
