@@ -352,17 +352,19 @@ def run_ours(args, world, rank, dev):
         e2e = run_e2e(layers, acts, cases, dev, world, max(1, min(args.steps, 5)))
 
     del graphs
-    standin = quant = None
+    standin = quant = standin_tp = None
     if not args.no_standin and world == 1:
         standin = run_standin(dev)
         quant = run_quantisers(dev)
+    if not args.no_standin and world > 1:
+        standin_tp = run_standin_tp(dev, rank, world)
 
     launches = args.steps * len(cases) * COPIES
     return {
         "value": round(value_us, 2), "ms_per_step": round(ms, 4), "per_shape": per_shape,
         "l2_warm_us": warm, "roofline": roofline, "roofline_other": other,
         "allgather_us_per_sweep": allgather_us, "e2e": e2e, "standin_us_per_layer": standin,
-        "quantisers": quant,
+        "quantisers": quant, "standin_tp_us_per_layer": standin_tp,
         "clocks": clocks.summary(), "gpu_launches": launches,
     }
 
@@ -414,6 +416,28 @@ def run_e2e(layers, acts, cases, dev, world, passes):
     return {"value": round(us, 2), "unit": "us", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "passes": passes,
             "note": "one eager pass over the sweep through int8_linear.w8a8_mm, host copies included"}
+
+
+def run_standin_tp(dev, rank, world):
+    """BASELINE config 4 under tensor parallelism: the stand-in decoder split over the
+    ranks (int8_linear/tp.py), µs per layer, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from int8_linear.standin import LAYERS, TPStandinDecoder
+
+    out = {}
+    for m in STANDIN_BATCHES:
+        s = TPStandinDecoder(m, rank, world, device=dev)
+        g = s.capture()
+        dist.barrier()
+        us = statistics.median([time_graph(g, windows=5) for _ in range(3)]) / LAYERS
+        t = torch.tensor([us], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[str(m)] = round(float(t.item()), 2)
+        del g, s
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_quantisers(dev):

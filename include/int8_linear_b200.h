@@ -185,6 +185,36 @@ int i8l_quant_rows(const void *x, int64_t ldx, int32_t act_dtype, int8_t *q,
                    int64_t ldq, float *scale, int32_t M, int32_t K,
                    int32_t precise_div, void *stream);
 
+/*
+ * The two quantisers above for a token row that is split across GPUs (the input of a
+ * row-parallel linear under tensor parallelism).  With absmax_out (M floats) each
+ * row's local max|y| is written and nothing is quantised; after the caller takes the
+ * MAX over the GPUs, the call with absmax_in quantises with that shared absmax, so
+ * each GPU's int8 values and scale are exactly those one GPU would compute for the
+ * whole row.  Both pointers NULL: same as i8l_silu_mul_quant / i8l_quant_rows.  No
+ * reference counterpart (the reference is single-GPU).
+ */
+int i8l_silu_mul_quant_ex(const void *gate_up, int64_t ld, int32_t act_dtype, int8_t *q,
+                          int64_t ldq, float *scale, int32_t M, int32_t I,
+                          int32_t precise_div, int32_t round_silu,
+                          const float *absmax_in, float *absmax_out, void *stream);
+int i8l_quant_rows_ex(const void *x, int64_t ldx, int32_t act_dtype, int8_t *q,
+                      int64_t ldq, float *scale, int32_t M, int32_t K,
+                      int32_t precise_div, const float *absmax_in, float *absmax_out,
+                      void *stream);
+
+/*
+ * out[M,N] = cast(((float(acc) * sa) * sb) + bias) for an int32 product computed
+ * elsewhere, e.g. the SUM over GPUs of a row-parallel layer's partial products: the
+ * GEMM epilogue's arithmetic, so the result equals a one-GPU i8l_w8a8_mm bit for bit.
+ * acc rows at lda, out rows at ldo (I8L_BF16/F16/F32).  Same role as the epilogue of
+ * the reference kernel (int8_linear/kernel.py:105-120).
+ */
+int i8l_dequant_i32(const int32_t *acc, int64_t lda, const float *sa, int32_t sa_per_row,
+                    const float *sb, int32_t sb_per_col, const void *bias,
+                    int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldo,
+                    int32_t M, int32_t N, void *stream);
+
 /* One-line message for the last non-OK return on this host thread. */
 const char *i8l_last_error(void);
 

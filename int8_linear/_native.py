@@ -47,6 +47,11 @@ SIGNATURES = {
                                      _i32, _i32, _f32, _i32, _vp]),
     "i8l_silu_mul_quant": (_i32, [_vp, _i64, _i32, _i8p, _i64, _fp, _i32, _i32, _i32, _i32, _vp]),
     "i8l_quant_rows": (_i32, [_vp, _i64, _i32, _i8p, _i64, _fp, _i32, _i32, _i32, _vp]),
+    "i8l_silu_mul_quant_ex": (_i32, [_vp, _i64, _i32, _i8p, _i64, _fp, _i32, _i32, _i32, _i32, _fp, _fp,
+                                     _vp]),
+    "i8l_quant_rows_ex": (_i32, [_vp, _i64, _i32, _i8p, _i64, _fp, _i32, _i32, _i32, _fp, _fp, _vp]),
+    "i8l_dequant_i32": (_i32, [_vp, _i64, _fp, _i32, _fp, _i32, _vp, _i32, _vp, _i32, _i64, _i32, _i32,
+                               _vp]),
     "i8l_last_error": (ctypes.c_char_p, []),
     "i8l_read_status": (_i32, [ctypes.POINTER(_i32)]),
     "i8l_clear_status": (_i32, []),

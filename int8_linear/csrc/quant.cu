@@ -115,15 +115,26 @@ __device__ __forceinline__ float round_to_weight(float v, int dtype) {
 // scale = absmax/127, inv = 127/absmax (0 for a zero row), q = rint(y*inv)
 // saturated to [-128, 127].  `y` holds this thread's values (0 where the thread
 // owns no column), `valid` marks the real ones.
+//
+// For rows split across GPUs: with amax_out the row's local absmax is written there and
+// nothing is quantised; with amax_in (e.g. the MAX over GPUs) that absmax is used in
+// place of the row's own, so every GPU quantises exactly as one GPU would.
 template <int NV, int VW>
 __device__ __forceinline__ void quantize_row(const float (&y)[NV][VW], int K, int8_t *qrow,
-                                             float *scale_out, int precise, float *red) {
+                                             float *scale_out, int precise, float *red,
+                                             const float *amax_in = nullptr,
+                                             float *amax_out = nullptr) {
   float amax = 0.f;
 #pragma unroll
   for (int v = 0; v < NV; ++v)
 #pragma unroll
     for (int i = 0; i < VW; ++i) amax = fmaxf(amax, fabsf(y[v][i]));
   amax = block_max(amax, red);
+  if (amax_out) {
+    if (threadIdx.x == 0) *amax_out = amax;
+    return;
+  }
+  if (amax_in) amax = *amax_in;
   const float scale = precise ? div_rn(amax, 127.f) : div_full(amax, 127.f);
   const float inv = amax == 0.f ? 0.f : (precise ? div_rn(127.f, amax) : div_full(127.f, amax));
   if (threadIdx.x == 0) *scale_out = scale;
@@ -215,6 +226,8 @@ __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) add_rmsnorm_quant_kernel
 }
 
 struct SiluArgs {
+  const float *amax_in;  // per row, or NULL
+  float *amax_out;       // per row, or NULL
   const void *gu;
   long long ld;
   int8_t *q;
@@ -254,10 +267,13 @@ __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) silu_mul_quant_kernel(co
       for (int i = 0; i < VW; ++i) y[v][i] = 0.f;
     }
   }
-  quantize_row<NV, VW>(y, a.I, a.q + row * a.ldq, a.scale + row, a.precise, red);
+  quantize_row<NV, VW>(y, a.I, a.q + row * a.ldq, a.scale + row, a.precise, red,
+                       a.amax_in ? a.amax_in + row : nullptr, a.amax_out ? a.amax_out + row : nullptr);
 }
 
 struct QuantArgs {
+  const float *amax_in;  // per row, or NULL
+  float *amax_out;       // per row, or NULL
   const void *x;
   long long ldx;
   int8_t *q;
@@ -286,7 +302,55 @@ __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) quant_rows_kernel(const 
       for (int i = 0; i < VW; ++i) y[v][i] = 0.f;
     }
   }
-  quantize_row<NV, VW>(y, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red);
+  quantize_row<NV, VW>(y, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red,
+                       a.amax_in ? a.amax_in + row : nullptr, a.amax_out ? a.amax_out + row : nullptr);
+}
+
+// Dequantisation of an int32 product computed elsewhere (e.g. summed over the GPUs of
+// a row-parallel layer): out = cast(((float(acc) * sa[m]) * sb[n]) + bias[n]), the same
+// fp32 steps as the GEMM epilogue, so the result matches a one-GPU GEMM bit for bit.
+struct DequantArgs {
+  const int *acc;
+  long long lda;
+  const float *sa;
+  int sa_per_row;
+  const float *sb;
+  int sb_per_col;
+  const void *bias;
+  int bias_dtype;
+  void *out;
+  int out_dtype;
+  long long ldo;
+  int M, N;
+};
+
+__global__ void __launch_bounds__(256) dequant_i32_kernel(const DequantArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const long long total = static_cast<long long>(a.M) * a.N;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+    const int m = static_cast<int>(i / a.N), n = static_cast<int>(i - static_cast<long long>(m) * a.N);
+    float v = __int2float_rn(a.acc[m * a.lda + n]);
+    v = __fmul_rn(v, a.sa_per_row ? a.sa[m] : a.sa[0]);
+    v = __fmul_rn(v, a.sb_per_col ? a.sb[n] : a.sb[0]);
+    if (a.bias) {
+      float b;
+      if (a.bias_dtype == I8L_BF16)
+        b = __bfloat162float(static_cast<const __nv_bfloat16 *>(a.bias)[n]);
+      else if (a.bias_dtype == I8L_F16)
+        b = __half2float(static_cast<const __half *>(a.bias)[n]);
+      else
+        b = static_cast<const float *>(a.bias)[n];
+      v = __fadd_rn(v, b);
+    }
+    const long long o = m * a.ldo + n;
+    if (a.out_dtype == I8L_BF16)
+      static_cast<__nv_bfloat16 *>(a.out)[o] = __float2bfloat16_rn(v);
+    else if (a.out_dtype == I8L_F16)
+      static_cast<__half *>(a.out)[o] = __float2half_rn(v);
+    else
+      static_cast<float *>(a.out)[o] = v;
+  }
 }
 
 // ------------------------------------------------------------------ launch
@@ -393,14 +457,25 @@ extern "C" int i8l_add_rmsnorm_quant(const void *x, int64_t ldx, const void *res
 extern "C" int i8l_silu_mul_quant(const void *gate_up, int64_t ld, int32_t act_dtype, int8_t *q,
                                   int64_t ldq, float *scale, int32_t M, int32_t I,
                                   int32_t precise_div, int32_t round_silu, void *stream) {
+  return i8l_silu_mul_quant_ex(gate_up, ld, act_dtype, q, ldq, scale, M, I, precise_div,
+                               round_silu, nullptr, nullptr, stream);
+}
+
+extern "C" int i8l_silu_mul_quant_ex(const void *gate_up, int64_t ld, int32_t act_dtype,
+                                     int8_t *q, int64_t ldq, float *scale, int32_t M, int32_t I,
+                                     int32_t precise_div, int32_t round_silu,
+                                     const float *absmax_in, float *absmax_out, void *stream) {
   int e = check_act(act_dtype);
   if (e) return e;
   if (M < 0 || I <= 0) return set_error(I8L_EINVAL, "bad size M=%d I=%d", M, I);
   if (M == 0) return I8L_OK;
-  if (!gate_up || !q || !scale) return set_error(I8L_EINVAL, "NULL pointer argument");
-  if (ld < 2LL * I || ldq < I) return set_error(I8L_EINVAL, "row stride too small");
-  SiluArgs a{gate_up, ld, q, ldq, scale, I, precise_div, round_silu};
-  const bool vec = I % 8 == 0 && ld % 8 == 0 && ldq % 8 == 0 && aligned16(gate_up) && aligned16(q);
+  if (!gate_up || (!absmax_out && (!q || !scale)))
+    return set_error(I8L_EINVAL, "NULL pointer argument");
+  if (absmax_in && absmax_out) return set_error(I8L_EINVAL, "absmax_in and absmax_out are exclusive");
+  if (ld < 2LL * I || (!absmax_out && ldq < I)) return set_error(I8L_EINVAL, "row stride too small");
+  SiluArgs a{absmax_in, absmax_out, gate_up, ld, q, ldq, scale, I, precise_div, round_silu};
+  const bool vec = I % 8 == 0 && ld % 8 == 0 && aligned16(gate_up) &&
+                   (absmax_out || (ldq % 8 == 0 && aligned16(q)));
   RowShape rs;
   if (!row_shape(I, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -425,14 +500,24 @@ extern "C" int i8l_silu_mul_quant(const void *gate_up, int64_t ld, int32_t act_d
 extern "C" int i8l_quant_rows(const void *x, int64_t ldx, int32_t act_dtype, int8_t *q,
                               int64_t ldq, float *scale, int32_t M, int32_t K,
                               int32_t precise_div, void *stream) {
+  return i8l_quant_rows_ex(x, ldx, act_dtype, q, ldq, scale, M, K, precise_div, nullptr, nullptr,
+                           stream);
+}
+
+extern "C" int i8l_quant_rows_ex(const void *x, int64_t ldx, int32_t act_dtype, int8_t *q,
+                                 int64_t ldq, float *scale, int32_t M, int32_t K,
+                                 int32_t precise_div, const float *absmax_in, float *absmax_out,
+                                 void *stream) {
   int e = check_act(act_dtype);
   if (e) return e;
   if (M < 0 || K <= 0) return set_error(I8L_EINVAL, "bad size M=%d K=%d", M, K);
   if (M == 0) return I8L_OK;
-  if (!x || !q || !scale) return set_error(I8L_EINVAL, "NULL pointer argument");
-  if (ldx < K || ldq < K) return set_error(I8L_EINVAL, "row stride smaller than K");
-  QuantArgs a{x, ldx, q, ldq, scale, K, precise_div};
-  const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldq % 8 == 0 && aligned16(x) && aligned16(q);
+  if (!x || (!absmax_out && (!q || !scale))) return set_error(I8L_EINVAL, "NULL pointer argument");
+  if (absmax_in && absmax_out) return set_error(I8L_EINVAL, "absmax_in and absmax_out are exclusive");
+  if (ldx < K || (!absmax_out && ldq < K)) return set_error(I8L_EINVAL, "row stride smaller than K");
+  QuantArgs a{absmax_in, absmax_out, x, ldx, q, ldq, scale, K, precise_div};
+  const bool vec = K % 8 == 0 && ldx % 8 == 0 && aligned16(x) &&
+                   (absmax_out || (ldq % 8 == 0 && aligned16(q)));
   RowShape rs;
   if (!row_shape(K, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -452,4 +537,25 @@ extern "C" int i8l_quant_rows(const void *x, int64_t ldx, int32_t act_dtype, int
     }
   }
   return finish_launch(err, "quant_rows launch");
+}
+
+extern "C" int i8l_dequant_i32(const int32_t *acc, int64_t lda, const float *sa, int32_t sa_per_row,
+                               const float *sb, int32_t sb_per_col, const void *bias,
+                               int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldo,
+                               int32_t M, int32_t N, void *stream) {
+  if (M < 0 || N < 0) return set_error(I8L_EINVAL, "bad size M=%d N=%d", M, N);
+  if (M == 0 || N == 0) return I8L_OK;
+  if (!acc || !sa || !sb || !out) return set_error(I8L_EINVAL, "NULL pointer argument");
+  if (out_dtype < I8L_BF16 || out_dtype > I8L_F32)
+    return set_error(I8L_ENOTSUP, "output dtype code %d not supported", out_dtype);
+  if (bias && (bias_dtype < I8L_BF16 || bias_dtype > I8L_F32))
+    return set_error(I8L_ENOTSUP, "bias dtype code %d not supported", bias_dtype);
+  if (lda < N || ldo < N) return set_error(I8L_EINVAL, "row stride smaller than N");
+  DequantArgs a{reinterpret_cast<const int *>(acc), lda, sa, sa_per_row, sb, sb_per_col, bias,
+                bias_dtype, out, out_dtype, ldo, M, N};
+  const long long total = static_cast<long long>(M) * N;
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  cudaError_t err = launch(dequant_i32_kernel, dim3(blocks), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), 1, a);
+  return finish_launch(err, "dequant_i32 launch");
 }

@@ -71,8 +71,11 @@ def add_rmsnorm_quant(x: torch.Tensor, residual: torch.Tensor | None, weight: to
     return q, s, rout
 
 
-def silu_mul_quant(gate_up: torch.Tensor, precise_div: bool = True, round_silu: bool = False):
-    """silu(gate) * up, quantised: (x_q int8 [M, I], scale fp32 [M, 1])."""
+def silu_mul_quant(gate_up: torch.Tensor, precise_div: bool = True, round_silu: bool = False,
+                   absmax: torch.Tensor | None = None):
+    """silu(gate) * up, quantised: (x_q int8 [M, I], scale fp32 [M, 1]).  `absmax` ([M]
+    float32, e.g. the MAX over the GPUs sharing each row) replaces each row's own
+    max|y|, as for a row split across GPUs (see silu_mul_absmax)."""
     assert gate_up.is_contiguous() and gate_up.dim() == 2
     M, I2 = gate_up.shape
     I = I2 // 2
@@ -80,27 +83,66 @@ def silu_mul_quant(gate_up: torch.Tensor, precise_div: bool = True, round_silu: 
     q = torch.empty((M, I), dtype=torch.int8, device=gate_up.device)
     s = torch.empty((M, 1), dtype=torch.float32, device=gate_up.device)
     if M and I:
-        _native.check(_native.load().i8l_silu_mul_quant(
+        amax = _absmax_arg(absmax, M)
+        _native.check(_native.load().i8l_silu_mul_quant_ex(
             gate_up.data_ptr(), gate_up.stride(0), act, q.data_ptr(), q.stride(0), s.data_ptr(),
-            M, I, int(bool(precise_div)), int(bool(round_silu)), _stream(gate_up)))
+            M, I, int(bool(precise_div)), int(bool(round_silu)),
+            amax.data_ptr() if amax is not None else None, None, _stream(gate_up)))
     return q, s
 
 
-def per_token_quant(x: torch.Tensor, precise_div: bool = True):
+def silu_mul_absmax(gate_up: torch.Tensor, round_silu: bool = False) -> torch.Tensor:
+    """max over each row of |silu(gate) * up| (float32 [M]), the first half of a
+    SiLU-and-mul quantisation whose row is split across GPUs."""
+    assert gate_up.is_contiguous() and gate_up.dim() == 2
+    M, I = gate_up.shape[0], gate_up.shape[1] // 2
+    act = _act_code(gate_up)
+    out = torch.empty((M,), dtype=torch.float32, device=gate_up.device)
+    if M and I:
+        _native.check(_native.load().i8l_silu_mul_quant_ex(
+            gate_up.data_ptr(), gate_up.stride(0), act, None, 0, None, M, I, 1,
+            int(bool(round_silu)), None, out.data_ptr(), _stream(gate_up)))
+    return out
+
+
+def _absmax_arg(absmax: torch.Tensor | None, m: int) -> torch.Tensor | None:
+    if absmax is None:
+        return None
+    absmax = absmax.reshape(-1).contiguous()
+    if absmax.dtype != torch.float32 or absmax.numel() != m:
+        raise ValueError(f"absmax must hold {m} float32 values, got {absmax.dtype} {tuple(absmax.shape)}")
+    return absmax
+
+
+def per_token_quant(x: torch.Tensor, precise_div: bool = True, absmax: torch.Tensor | None = None):
     """Dynamic symmetric per-token int8 quantisation of a 2-D activation whose rows
     are contiguous (a column slice of a wider matrix is fine, no copy is made):
     (x_q int8 [M, K], scale fp32 [M, 1]).  This is the step the reference leaves to
-    vLLM's scaled_int8_quant before o_proj (bench/fuse_quant.py:234)."""
+    vLLM's scaled_int8_quant before o_proj (bench/fuse_quant.py:234).  `absmax`
+    ([M] float32) replaces each row's own max|x|, for rows split across GPUs."""
     assert x.dim() == 2 and x.stride(1) == 1
     M, K = x.shape
     act = _act_code(x)
     q = torch.empty((M, K), dtype=torch.int8, device=x.device)
     s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
     if M and K:
-        _native.check(_native.load().i8l_quant_rows(
+        amax = _absmax_arg(absmax, M)
+        _native.check(_native.load().i8l_quant_rows_ex(
             x.data_ptr(), x.stride(0), act, q.data_ptr(), q.stride(0), s.data_ptr(), M, K,
-            int(bool(precise_div)), _stream(x)))
+            int(bool(precise_div)), amax.data_ptr() if amax is not None else None, None, _stream(x)))
     return q, s
+
+
+def row_absmax(x: torch.Tensor) -> torch.Tensor:
+    """max over each row of |x| (float32 [M]) for a bf16/fp16 matrix with contiguous rows."""
+    assert x.dim() == 2 and x.stride(1) == 1
+    M, K = x.shape
+    act = _act_code(x)
+    out = torch.empty((M,), dtype=torch.float32, device=x.device)
+    if M and K:
+        _native.check(_native.load().i8l_quant_rows_ex(
+            x.data_ptr(), x.stride(0), act, None, 0, None, M, K, 1, None, out.data_ptr(), _stream(x)))
+    return out
 
 
 # Numerics the custom ops use.  The reference measures which choice matches vLLM and

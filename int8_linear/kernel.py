@@ -252,3 +252,27 @@ def _launch(lib, a, w, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, str
         _DTYPE_CODE[bias.dtype] if bias is not None else 0,
         out.data_ptr(), _native.I32 if raw else _DTYPE_CODE[out_dtype], out.stride(0),
         m, n, k, ctypes.byref(tile), ws.data_ptr(), ws.numel(), stream)
+
+
+def dequant_i32(acc: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+                out_dtype: torch.dtype = torch.bfloat16, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """cast(((float(acc) * scale_a) * scale_b) + bias) for an int32 [M, N] product made
+    elsewhere (e.g. summed over the GPUs of a row-parallel layer): the GEMM epilogue's
+    arithmetic, so the result equals w8a8_mm on the whole product bit for bit."""
+    if acc.dtype != torch.int32 or acc.dim() != 2 or acc.stride(1) != 1:
+        raise ValueError("acc must be a 2-D int32 tensor with contiguous rows")
+    m, n = acc.shape
+    sa, sb = scale_a.reshape(-1).contiguous(), scale_b.reshape(-1).contiguous()
+    if sa.numel() not in (1, m) or sb.numel() not in (1, n):
+        raise ValueError(f"scale sizes {sa.numel()} and {sb.numel()} fit neither {m} nor {n}")
+    if out_dtype not in _DTYPE_CODE or (bias is not None and bias.dtype not in _DTYPE_CODE):
+        raise NotSupported("bf16/fp16/fp32 output and bias only")
+    bias = bias.contiguous() if bias is not None else None
+    out = torch.empty((m, n), dtype=out_dtype, device=acc.device)
+    if m and n:
+        _native.check(_native.load().i8l_dequant_i32(
+            acc.data_ptr(), acc.stride(0), sa.data_ptr(), int(sa.numel() > 1), sb.data_ptr(),
+            int(sb.numel() > 1), bias.data_ptr() if bias is not None else None,
+            _DTYPE_CODE[bias.dtype] if bias is not None else 0, out.data_ptr(), _DTYPE_CODE[out_dtype],
+            out.stride(0), m, n, torch.cuda.current_stream(acc.device).cuda_stream))
+    return out

@@ -100,3 +100,58 @@ class StandinDecoder:
     def weight_bytes(self) -> int:
         return sum(lin.w_t.numel() + lin.scale.numel() * 4 for layer in self.layers
                    for lin in layer.values())
+
+
+class TPStandinDecoder:
+    """The stand-in decoder split over `world` GPUs, Megatron-style (int8_linear/tp.py):
+    qkv and gate_up column-parallel (q, k, v and gate, up sharded separately), o_proj and
+    down row-parallel with an exact int32 all-reduce, the row-split activations quantised
+    with the global per-token absmax.  Built from the same seeded weights as
+    StandinDecoder, so every rank's output equals the one-GPU output bit for bit."""
+
+    def __init__(self, m: int, rank: int, world: int, group=None, layers: int = LAYERS,
+                 seed: int = 0, device="cuda"):
+        from int8_linear import tp
+
+        full = StandinDecoder(m, layers=layers, seed=seed, device=device)
+        self.x, self.w = full.x, full.w
+        self.world, self.group = world, group
+        self.layers = []
+        for layer in full.layers:
+            qkv, o, gu, dn = (layer[k] for k in ("qkv_proj", "o_proj", "gate_up_proj", "down_proj"))
+            qkv_parts = (HIDDEN, (qkv.w_t.shape[1] - HIDDEN) // 2, (qkv.w_t.shape[1] - HIDDEN) // 2)
+            self.layers.append({
+                "qkv": tp.ColumnParallelW8A8(tp.shard_rows_of(qkv.w_t.t(), rank, world, qkv_parts),
+                                             tp.shard_rows_of(qkv.scale, rank, world, qkv_parts),
+                                             group=group),
+                "o": tp.RowParallelW8A8(tp.shard_cols_of(o.w_t.t(), rank, world), o.scale, group=group),
+                "gu": tp.ColumnParallelW8A8(tp.shard_rows_of(gu.w_t.t(), rank, world, (INTER, INTER)),
+                                            tp.shard_rows_of(gu.scale, rank, world, (INTER, INTER)),
+                                            group=group),
+                "dn": tp.RowParallelW8A8(tp.shard_cols_of(dn.w_t.t(), rank, world), dn.scale, group=group),
+            })
+        del full
+        torch.cuda.empty_cache()
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.out: torch.Tensor | None = None
+
+    def step(self) -> torch.Tensor:
+        from int8_linear import tp
+
+        res = self.x
+        q, s, _ = add_rmsnorm_quant(self.x, None, self.w, EPS)
+        h = None
+        q_cols = HIDDEN // self.world
+        for i, layer in enumerate(self.layers):
+            if i:
+                q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
+            qkv = layer["qkv"](q, s)                  # [M, 4096/g]: this rank's q | k | v
+            q, s = tp.sharded_per_token_quant(qkv[:, :q_cols], group=self.group)
+            h = layer["o"](q, s)                      # int32 all-reduce, dequantised once
+            q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
+            gu = layer["gu"](q, s)                    # [M, 12288/g]: this rank's gate | up
+            q, s = tp.sharded_silu_mul_quant(gu, group=self.group)
+            h = layer["dn"](q, s)
+        return h
+
+    capture = StandinDecoder.capture

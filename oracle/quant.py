@@ -34,11 +34,15 @@ def quant(y: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     return q, (absmax / np.float32(127.0)).astype(np.float32)
 
 
-def quant_ieee(y: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+def quant_ieee(y: np.ndarray, absmax: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
     """The reference KERNEL's row quantiser with precise_div (int8_linear/fused_quant.py:
-    41-53): inv = div_rn(127, absmax), one IEEE rounding; otherwise as `quant`."""
+    41-53): inv = div_rn(127, absmax), one IEEE rounding; otherwise as `quant`.  A given
+    `absmax` (one per row) replaces the row's own, as for a row split across GPUs."""
     yf = np.asarray(y, dtype=np.float32)
-    absmax = np.abs(yf).max(axis=-1, keepdims=True)
+    if absmax is None:
+        absmax = np.abs(yf).max(axis=-1, keepdims=True)
+    else:
+        absmax = np.asarray(absmax, np.float32).reshape(-1, 1)
     with np.errstate(divide="ignore"):
         inv = np.where(absmax == 0, np.float32(0), np.float32(127.0) / absmax).astype(np.float32)
     q = np.clip(np.rint(yf * inv), -128, 127).astype(np.int8)

@@ -208,3 +208,20 @@ def test_empty_batch():
 
 def test_choose_config_is_per_shape():
     assert choose_config(1, 4096, 2048).swapped and not choose_config(4096, 4096, 2048).swapped
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("m,k,n", [(1, 2048, 2048), (37, 1024, 1000), (300, 512, 4096)])
+def test_dequant_i32_equals_the_gemm_epilogue(dtype, m, k, n):
+    """The standalone epilogue on an int32 product (the row-parallel path) equals the
+    fused GEMM bit for bit."""
+    from int8_linear.kernel import dequant_i32
+
+    a, w = ints((m, k), 60), ints((n, k), 61)
+    g = torch.Generator().manual_seed(62)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = torch.randn(n, generator=g).to(dtype).cuda()
+    acc = w8a8_mm(a, w.t(), one(), one(), raw=True)
+    got = dequant_i32(acc, sa, sb, dtype, bias)
+    assert torch.equal(got, w8a8_mm(a, w.t(), sa, sb, dtype, bias))

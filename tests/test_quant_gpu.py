@@ -136,3 +136,31 @@ def test_prequant_matmul_matches_unfused():
     pq = vfp.PreQuant(q, s, torch.bfloat16)
     out = w8a8_mm(pq.data, w.t(), pq.scale, ws, pq.dtype)
     assert out.shape == (5, 2048) and torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("m,k", [(1, 2048), (33, 1024), (7, 1000)])
+def test_split_row_quantisation_with_a_given_absmax(m, k):
+    """row_absmax / silu_mul_absmax and quantising with a given absmax (the pieces of a
+    row split across GPUs) reproduce the whole-row quantiser."""
+    x = rand((m, k), 40, 3.0)
+    amax = fq.row_absmax(x)
+    assert torch.equal(amax, np_t(x).abs().amax(-1))
+    q, s = fq.per_token_quant(x, absmax=amax)
+    q0, s0 = fq.per_token_quant(x)
+    assert torch.equal(q, q0) and torch.equal(s, s0)
+    # a larger absmax (another GPU's half of the row) scales the same way the oracle does
+    big = amax * 1.5
+    q, s = fq.per_token_quant(x, absmax=big)
+    qo, so = oq.quant_ieee(np_(x), np_(big))
+    check(q, s, qo, so, exact=True)
+    gu = rand((m, 2 * k), 41, 2.0)
+    amax = fq.silu_mul_absmax(gu, round_silu=True)
+    q, s = fq.silu_mul_quant(gu, True, True, absmax=amax)
+    q0, s0 = fq.silu_mul_quant(gu, True, True)
+    assert torch.equal(q, q0) and torch.equal(s, s0)
+    # scale = absmax / 127 with an IEEE divide (numpy's float32 division)
+    assert np.array_equal(np_(s).reshape(-1), (np_(amax) / np.float32(127.0)).astype(np.float32))
+
+
+def np_t(x):
+    return x.float()
