@@ -57,7 +57,11 @@ extern "C" {
  *                workspace);
  *   cluster:     CTAs per cluster for split = 3 (0 = the library's choice, <= 8);
  *   store:       output path: 0 = the library's choice, 1 = TMA stores through
- *                shared memory, 2 = plain stores.
+ *                shared memory, 2 = plain stores;
+ *   act:         activation path of swap_ab tiles: 0 = the library's choice, 1 = TMA
+ *                loads, 2 = plain loads by the epilogue warps straight after the
+ *                dependency wait (needs M <= tok_tile, one tile or cluster segment
+ *                per CTA, and that segment's k-blocks all in the ring at once).
  */
 typedef struct i8l_tile {
   int32_t swap_ab;
@@ -69,6 +73,7 @@ typedef struct i8l_tile {
   int32_t split;
   int32_t cluster;
   int32_t store;
+  int32_t act;
 } i8l_tile;
 
 /*

@@ -26,7 +26,8 @@ class I8LTile(ctypes.Structure):
     """Mirror of struct i8l_tile."""
 
     _fields_ = [(name, ctypes.c_int32) for name in (
-        "swap_ab", "tok_tile", "w_tile", "stages", "ctas", "group", "split", "cluster", "store")]
+        "swap_ab", "tok_tile", "w_tile", "stages", "ctas", "group", "split", "cluster", "store",
+        "act")]
 
 
 _lib = None

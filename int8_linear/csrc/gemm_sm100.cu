@@ -66,6 +66,13 @@ struct GemmArgs {
   int *status;
   int cluster;    // >1: the CTAs of each cluster split K of one tile (reduced over DSMEM)
   int cluster_early;  // contributors push into the leader's staging area without waiting
+  // Direct activation loads (swap tiles holding every token, one segment per CTA whose
+  // k-blocks all fit in the ring): the epilogue warps copy A's k-blocks into the ring's
+  // Y slots with plain loads after the dependency wait, so the activation never queues
+  // in the SM's TMA unit behind weight prefetches; the producer loads only weights.
+  int act_direct;
+  const int8_t *act;
+  long long lda;
 };
 
 struct Segment {
@@ -79,16 +86,23 @@ struct Schedule {
   int dp_next;
   long long it, it_end;
 
+  // Each role initialises its copy before the dependency wait: the divisions here
+  // (64-bit ones for stream-K) then overlap the previous kernel instead of delaying
+  // the first load after the wait.
   __device__ __forceinline__ void init(const GemmArgs &a) {
     if (a.cluster > 1) {
       // One tile per cluster; CTA rank r takes the r-th of `cluster` equal k ranges.
       const int r = static_cast<int>(blockIdx.x) % a.cluster;
       dp_next = static_cast<int>(blockIdx.x) / a.cluster;
-      it = static_cast<long long>(a.kblocks) * r / a.cluster;
-      it_end = static_cast<long long>(a.kblocks) * (r + 1) / a.cluster;
+      it = a.kblocks * r / a.cluster;
+      it_end = a.kblocks * (r + 1) / a.cluster;
       return;
     }
     dp_next = blockIdx.x;
+    if (a.sk_iters == 0) {
+      it = it_end = 0;
+      return;
+    }
     const long long g = gridDim.x;
     it = a.sk_iters * static_cast<long long>(blockIdx.x) / g;
     it_end = a.sk_iters * static_cast<long long>(blockIdx.x + 1) / g;
@@ -141,6 +155,11 @@ __device__ __forceinline__ int split_slot(const GemmArgs &a, int tile) {
 // run at the same time share Y tiles in L2.
 __device__ __forceinline__ void tile_coords(const GemmArgs &a, int t, int &tx,
                                             int &ty) {
+  if (a.tiles_y == 1) {  // one Y tile (a decode batch): no divisions
+    tx = t;
+    ty = 0;
+    return;
+  }
   const int per_group = a.group * a.tiles_y;
   const int g = t / per_group;
   const int first = g * a.group;
@@ -204,43 +223,44 @@ __device__ __forceinline__ void store_elem(void *out, int dtype, long long idx,
   }
 }
 
-// Direct-store fallback (output not TMA-addressable): stores 16 accumulator
-// values of TMEM lane `row` for accumulator columns c0..c0+15 with plain stores.
+// Everything one epilogue thread needs about the current tile.
+struct TileCtx {
+  int tx, ty, ncols;
+  uint32_t taddr;     // TMEM address of this warp's lanes in the accumulator
+  const float *s_col; // per accumulator column: sb (normal) or sa (swap), smem
+  const float *b_col; // per accumulator column: bias (normal), smem
+  float s_row, b_row; // per TMEM lane: sa (normal) or sb, bias (swap)
+};
+
+// Plain stores of 16 accumulator values of TMEM lane `row`, accumulator columns
+// c0..c0+15 (output not TMA-addressable, or few output rows).  The scales and bias
+// come from the tile context, fetched before the accumulator was ready.
 template <int TN>
-__device__ __forceinline__ void epilogue_direct(const GemmArgs &a, int tx, int ty,
-                                                int row, int c0,
-                                                const uint32_t (&r)[16]) {
+__device__ __forceinline__ void epilogue_direct(const GemmArgs &a, const TileCtx &t, int row,
+                                                int c0, const uint32_t (&r)[16]) {
   const bool raw = a.out_dtype == I8L_I32;
   const bool has_bias = a.bias != nullptr;
   if (a.swap) {
-    const int n = tx * kXRows + row;
+    const int n = t.tx * kXRows + row;
     if (n >= a.N) return;
-    const float sb = raw ? 0.f : (a.sb_per_col ? a.sb[n] : a.sb[0]);
-    const float bias = (!raw && has_bias) ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f;
-    const int m0 = ty * TN + c0;
+    const int m0 = t.ty * TN + c0;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int m = m0 + j;
       if (m < a.M) {
         const int acc = static_cast<int>(r[j]);
-        float v = 0.f;
-        if (!raw) v = dequant(acc, a.sa_per_row ? a.sa[m] : a.sa[0], sb, bias, has_bias);
+        const float v = raw ? 0.f : dequant(acc, t.s_col[c0 + j], t.s_row, t.b_row, has_bias);
         store_elem(a.out, a.out_dtype, static_cast<long long>(m) * a.ldc + n, acc, v);
       }
     }
   } else {
-    const int m = tx * kXRows + row;
+    const int m = t.tx * kXRows + row;
     if (m >= a.M) return;
-    const int n0 = ty * TN + c0;
+    const int n0 = t.ty * TN + c0;
     const long long base = static_cast<long long>(m) * a.ldc + n0;
-    const float sa = raw ? 0.f : (a.sa_per_row ? a.sa[m] : a.sa[0]);
     for (int j = 0; j < 16 && n0 + j < a.N; ++j) {
-      const int n = n0 + j;
       const int acc = static_cast<int>(r[j]);
-      float v = 0.f;
-      if (!raw)
-        v = dequant(acc, sa, a.sb_per_col ? a.sb[n] : a.sb[0],
-                    has_bias ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f, has_bias);
+      const float v = raw ? 0.f : dequant(acc, t.s_row, t.s_col[c0 + j], t.b_col[c0 + j], has_bias);
       store_elem(a.out, a.out_dtype, base + j, acc, v);
     }
   }
@@ -259,6 +279,16 @@ __device__ __forceinline__ int ld_cg_s32(const int *p) {
   return v;
 }
 
+// 16 bytes from global memory through L2 only (never a stale L1 line).
+__device__ __forceinline__ uint4 ld_cg_v4(const int8_t *p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_cg_s32(int *p, int v) {
   asm volatile("st.global.cg.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -272,14 +302,40 @@ template <int TN>
 struct SmemLayout {
   static constexpr int kYBytes = TN * kBK;
   static constexpr int kStageBytes = kXBytes + kYBytes;
-  static constexpr int kTmemCols = (2 * TN < 32) ? 32 : 2 * TN;
+  // Decode tiles rotate their k-steps over several accumulators: a chain of
+  // accumulating MMAs into the same columns runs one MMA at a time, and an N=16 MMA
+  // is far too short to hide that latency.  The epilogue adds the chains (int32
+  // addition is exact and order-free).  Two accumulators (double buffer) x chains.
+  static constexpr int kChains = TN <= 16 ? 4 : (TN <= 64 ? 2 : 1);
+  static constexpr int kAccCols = kChains * TN;
+  static constexpr int kTmemCols = (2 * kAccCols < 32) ? 32 : 2 * kAccCols;
   // stages | staging | scales | barriers: full[S], empty[S], acc_full[2],
-  // acc_empty[2], drain, peer, done | tmem slot, flags
+  // acc_empty[2], drain, peer, done, act | tmem slot, flags
   static size_t bytes(int stages) {
     return 1024 /* alignment slack */ + static_cast<size_t>(stages) * kStageBytes +
-           kStagingBytes + kScalBytes + static_cast<size_t>(2 * stages + 7) * 8 + 64;
+           kStagingBytes + kScalBytes + static_cast<size_t>(2 * stages + 8) * 8 + 64;
   }
 };
+
+// Accumulator columns c..c+15 of this warp's TMEM lanes, summed over the k-step
+// chains (chain j at taddr + j*TN).
+template <int TN>
+__device__ __forceinline__ void tmem_acc16(uint32_t taddr, int c, uint32_t (&r)[16]) {
+  constexpr int kChains = SmemLayout<TN>::kChains;
+  tmem_ld16(taddr + c, r);
+  if constexpr (kChains > 1) {
+    uint32_t q[kChains - 1][16];
+#pragma unroll
+    for (int j = 1; j < kChains; ++j) tmem_ld16(taddr + j * TN + c, q[j - 1]);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 1; j < kChains; ++j)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) r[i] += q[j - 1][i];
+  } else {
+    tmem_ld_wait();
+  }
+}
 
 // A warp's two 2 KB staging buffers for TMA stores / reduces; lane 0 owns the
 // bulk groups.  acquire() returns a buffer no bulk operation still reads.
@@ -299,15 +355,6 @@ struct Staging {
     if (lane == 0) bulk_wait<0>();
     __syncwarp();
   }
-};
-
-// Everything one epilogue thread needs about the current tile.
-struct TileCtx {
-  int tx, ty, ncols;
-  uint32_t taddr;     // TMEM address of this warp's lanes in the accumulator
-  const float *s_col; // per accumulator column: sb (normal) or sa (swap), smem
-  const float *b_col; // per accumulator column: bias (normal), smem
-  float s_row, b_row; // per TMEM lane: sa (normal) or sb, bias (swap)
 };
 
 // Writes 16 values (columns c0..c0+15 of this thread's TMEM lane) through the
@@ -391,6 +438,41 @@ __device__ __forceinline__ void emit_normal(const GemmArgs &a, const CUtensorMap
   }
 }
 
+// Direct activation loads: k-blocks kb0..kb1-1 of A (all TN token rows; rows past M
+// and columns past K read as zero, as the TMA zero fill gives) into Y slots 0.. of
+// the ring, each [TN rows][128 B] with the 128-byte swizzle of the TMA operand map
+// (16-byte chunk c of row r at chunk c ^ (r & 7)).  Each thread issues up to eight
+// 16-byte L2 loads before its first shared store, so their latencies overlap.
+template <int TN>
+__device__ __forceinline__ void load_act_direct(const GemmArgs &a, uint8_t *sy, int kb0, int kb1,
+                                                int tid) {
+  constexpr int kChunks = TN * (kBK / 16);
+  constexpr int kThr = kEpiWarps * 32;
+  const int n = (kb1 - kb0) * kChunks;
+  for (int base = tid; base < n; base += 8 * kThr) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int id = base + u * kThr;
+      v[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (id < n) {
+        const int j = id / kChunks, r = (id % kChunks) >> 3, c = id & 7;
+        const long long col = static_cast<long long>(kb0 + j) * kBK + c * 16;
+        if (r < a.M && col < a.K) v[u] = ld_cg_v4(a.act + static_cast<long long>(r) * a.lda + col);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int id = base + u * kThr;
+      if (id < n) {
+        const int j = id / kChunks, r = (id % kChunks) >> 3, c = id & 7;
+        *reinterpret_cast<uint4 *>(sy + static_cast<size_t>(j) * (TN * kBK) + r * kBK +
+                                   ((c ^ (r & 7)) << 4)) = v[u];
+      }
+    }
+  }
+}
+
 // Decode tiles (TN <= 64) cap registers so two CTAs fit on an SM: with programmatic
 // dependent launch the next GEMM's CTA streams its weights beside this one.
 template <int TN>
@@ -415,7 +497,8 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
   uint64_t *drain = acc_empty + 2;
   uint64_t *peer_bar = drain + 1;  // cluster leader: contributors' partial sums have landed
   uint64_t *done_bar = drain + 2;  // cluster contributor: the leader's ring is free for them
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 3);
+  uint64_t *act_bar = drain + 3;   // direct activation loads have landed in the Y slots
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   volatile int *last_flag = abort_flag + 1;
 
@@ -434,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     mbar_init(drain, 1);
     mbar_init(peer_bar, 1);
     mbar_init(done_bar, 1);
+    mbar_init(act_bar, kEpiWarps);
     if (a.cluster_early && cluster_ctarank() == 0) {
       // One tile per cluster: its partial sums arrive as (cluster-1) slots of the
       // live column chunks.  Armed before the cluster sync, so before any byte lands.
@@ -485,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           int tx, ty;
           tile_coords(a, sg.tile, tx, ty);
           for (int kb = sg.kb0; kb < sg.kb1 && pre < S; ++kb, ++pre) {
-            mbar_arrive_expect_tx(&full[pre], L::kStageBytes);
+            mbar_arrive_expect_tx(&full[pre], a.act_direct ? kXBytes : L::kStageBytes);
             if (a.swap)
               tma_load_2d(sx + static_cast<size_t>(pre) * kXBytes, &map_x, &full[pre], kb * kBK,
                           tx * kXRows, pol_x);
@@ -495,9 +579,9 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           }
         }
       }
-      pdl_wait();
       Schedule sch;
       sch.init(a);
+      pdl_wait();
       Segment seg;
       int stage = 0;
       uint32_t phase = 0;
@@ -508,8 +592,10 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
         tile_coords(a, seg.tile, tx, ty);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
           if (issued < pre) {
-            // Stage already claimed above with its weight tile: add the activation.
-            if (a.swap)
+            // Stage already claimed above with its weight tile: add the activation
+            // (with direct activation loads the epilogue warps fill the Y slot).
+            if (a.act_direct) {
+            } else if (a.swap)
               tma_load_2d(sy + static_cast<size_t>(stage) * L::kYBytes, &map_y, &full[stage],
                           kb * kBK, ty * TN, pol_y);
             else
@@ -568,8 +654,14 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           ok = false;
           break;
         }
+        if (a.act_direct && !issued_any &&
+            !mbar_wait_bounded(act_bar, 0, abort_flag, a.status, kStatusMmaWait)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * TN);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * L::kAccCols);
+        int kstep = 0;
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, a.status,
                                  kStatusMmaWait)) {
@@ -580,8 +672,11 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           const uint64_t ad = sw128_kmajor_desc(smem_u32(sx + static_cast<size_t>(stage) * kXBytes));
           const uint64_t bd = sw128_kmajor_desc(smem_u32(sy + static_cast<size_t>(stage) * L::kYBytes));
 #pragma unroll
-          for (int k = 0; k < kBK / 32; ++k)
-            mma_i8(d, ad + 2 * k, bd + 2 * k, kIdesc, (kb > seg.kb0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kBK / 32; ++k, ++kstep) {
+            const int ch = kstep % L::kChains;
+            mma_i8(d + static_cast<uint32_t>(ch * TN), ad + 2 * k, bd + 2 * k, kIdesc,
+                   kstep >= L::kChains ? 1u : 0u);
+          }
           issued_any = true;
           mma_commit(&empty[stage]);
           if (++stage == S) {
@@ -605,24 +700,33 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    pdl_wait();  // scales, outputs and the workspace belong to the stream's order
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const int epi_tid = threadIdx.x - 64;
+    Schedule sch;
+    sch.init(a);
+    Segment seg;
+    pdl_wait();  // scales, outputs and the workspace belong to the stream's order
+    if (a.act_direct) {
+      Schedule s0 = sch;
+      Segment g0;
+      if (s0.next(a, g0)) load_act_direct<TN>(a, sy, g0.kb0, g0.kb1, epi_tid);
+      fence_proxy_async_smem();  // generic-proxy stores -> operands of tcgen05.mma
+      __syncwarp();
+      if (lane == 0) mbar_arrive(act_bar);
+    }
     const bool raw = a.out_dtype == I8L_I32;
     const bool has_bias = a.bias != nullptr;
     const bool wide = a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16;
     Staging st{staging + static_cast<size_t>(quarter) * 2 * kStageBufBytes, 0u};
-    Schedule sch;
-    sch.init(a);
-    Segment seg;
     int acc = 0;
     uint32_t acc_phase = 0;
     while (sch.next(a, seg)) {
       TileCtx t;
       tile_coords(a, seg.tile, t.tx, t.ty);
       t.ncols = live_cols<TN>(a, t.ty);
-      t.taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * TN);
+      t.taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                static_cast<uint32_t>(acc * L::kAccCols);
       // Scales and bias for this tile, fetched before the accumulator is ready.
       float *s_col = scal + acc * kScalFloats;
       float *b_col = scal + 2 * kScalFloats + acc * kScalFloats;
@@ -679,8 +783,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
               smem_u32(ring + (static_cast<size_t>(rank) - 1) * TN * kXRows + row * TN), 0);
           for (int c = 0; c < nch; ++c) {
             uint32_t r[16];
-            tmem_ld16(t.taddr + c * 16, r);
-            tmem_ld_wait();
+            tmem_acc16<TN>(t.taddr, c * 16, r);
             if (go) {
 #pragma unroll
               for (int v = 0; v < 4; ++v)
@@ -701,8 +804,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
                                                                       kStatusClusterWait));
           for (int c0 = 0; c0 < t.ncols; c0 += 16) {
             uint32_t r[16];
-            tmem_ld16(t.taddr + c0, r);
-            tmem_ld_wait();
+            tmem_acc16<TN>(t.taddr, c0, r);
             if (c0 + 16 >= t.ncols) {
               tc_fence_before();
               __syncwarp();
@@ -724,16 +826,15 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
             if (a.tma_out)
               emit_swap16<TN>(a, &map_out, t, quarter, lane, c0, r, st);
             else
-              epilogue_direct<TN>(a, t.tx, t.ty, row, c0, r);
+              epilogue_direct<TN>(a, t, row, c0, r);
           }
         }
       } else if (whole) {
         if (!a.tma_out) {
           for (int c0 = 0; c0 < t.ncols; c0 += 16) {
             uint32_t r[16];
-            tmem_ld16(t.taddr + c0, r);
-            tmem_ld_wait();
-            epilogue_direct<TN>(a, t.tx, t.ty, row, c0, r);
+            tmem_acc16<TN>(t.taddr, c0, r);
+            epilogue_direct<TN>(a, t, row, c0, r);
           }
           tc_fence_before();
           __syncwarp();
@@ -741,8 +842,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
         } else if (a.swap) {
           for (int c0 = 0; c0 < t.ncols; c0 += 16) {
             uint32_t r[16];
-            tmem_ld16(t.taddr + c0, r);
-            tmem_ld_wait();
+            tmem_acc16<TN>(t.taddr, c0, r);
             if (c0 + 16 >= t.ncols) {
               tc_fence_before();
               __syncwarp();
@@ -754,9 +854,8 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           const int step = wide ? 32 : 16;
           for (int c0 = 0; c0 < t.ncols; c0 += step) {
             uint32_t r0[16], r1[16];
-            tmem_ld16(t.taddr + c0, r0);
-            if (wide) tmem_ld16(t.taddr + c0 + 16, r1);
-            tmem_ld_wait();
+            tmem_acc16<TN>(t.taddr, c0, r0);
+            if (wide) tmem_acc16<TN>(t.taddr, c0 + 16, r1);
             if (c0 + step >= t.ncols) {
               tc_fence_before();
               __syncwarp();
@@ -771,8 +870,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
         const int slot = split_slot(a, seg.tile);
         for (int c0 = 0; c0 < t.ncols; c0 += 16) {
           uint32_t r[16];
-          tmem_ld16(t.taddr + c0, r);
-          tmem_ld_wait();
+          tmem_acc16<TN>(t.taddr, c0, r);
           if (c0 + 16 >= t.ncols) {
             tc_fence_before();
             __syncwarp();
@@ -824,7 +922,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
               }
             }
             if (!a.tma_out)
-              epilogue_direct<TN>(a, t.tx, t.ty, row, c0, r0);
+              epilogue_direct<TN>(a, t, row, c0, r0);
             else if (a.swap)
               emit_swap16<TN>(a, &map_out, t, quarter, lane, c0, r0, st);
             else
@@ -911,7 +1009,7 @@ static int make_map(CUtensorMap *map, CUtensorMapDataType type, const void *ptr,
   return I8L_OK;
 }
 
-static size_t smem_extra() { return 1024 + kStagingBytes + kScalBytes + 7 * 8 + 64; }
+static size_t smem_extra() { return 1024 + kStagingBytes + kScalBytes + 8 * 8 + 64; }
 
 // Shared memory of one of two CTAs that share an SM (228 KB minus 1 KB reserved per CTA).
 constexpr int kHalfSmem = 233472 / 2 - 1024;
@@ -982,6 +1080,8 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
       if (user->group) t.group = user->group;
       t.split = user->split;
       t.cluster = user->cluster;
+      t.store = user->store;
+      t.act = user->act;
     }
   } else {
     t = *user;
@@ -1075,6 +1175,20 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   t.cluster = p->cluster;
   t.ctas = ctas;
   p->ctas = ctas;
+  // Direct activation loads: every token in one Y tile, one segment per CTA, and that
+  // segment's k-blocks all in the ring at once.
+  {
+    const int seg_kb = p->cluster > 1 ? (p->kblocks + p->cluster - 1) / p->cluster : p->kblocks;
+    const bool one_segment = p->cluster > 1 || (split == 1 && ctas >= p->total_tiles);
+    const bool direct_ok = t.swap_ab && p->tiles_y == 1 && one_segment && seg_kb <= t.stages;
+    if (t.act == 2 && !direct_ok)
+      return set_error(I8L_ENOTSUP,
+                       "direct activation loads need swap_ab, M <= tok_tile, one tile or cluster "
+                       "segment per CTA and at most `stages` k-blocks per CTA");
+    if (t.act < 0 || t.act > 2)
+      return set_error(I8L_ENOTSUP, "act mode %d unknown (0 auto, 1 TMA, 2 direct loads)", t.act);
+    t.act = (t.act == 2 || (t.act == 0 && direct_ok)) ? 2 : 1;
+  }
   p->sk_iters = p->cluster > 1 ? 0 : static_cast<long long>(p->total_tiles - p->dp_tiles) * p->kblocks;
   p->slots = p->sk_iters > 0 ? std::max(1, ctas - 1) : 0;
   const size_t counters_bytes = ((static_cast<size_t>(p->slots) * 4 + 255) / 256) * 256;
@@ -1225,6 +1339,9 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   }
   a.status = status_ptr();
   a.cluster = p.cluster;
+  a.act_direct = p.tile.act == 2 ? 1 : 0;
+  a.act = A;
+  a.lda = lda;
   // Early cluster mode needs the (cluster-1) slots, each TN x 128 int32 apart, inside
   // the leader's staging area, which plain stores leave unused.
   if (p.cluster > 1 && !a.tma_out)

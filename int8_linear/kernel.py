@@ -59,6 +59,9 @@ class Config:
     ctas    persistent CTAs, 0 for one per SM.
     cluster CTAs per cluster for split=3, 0 for the library's choice.
     store   output path: 0 the library's choice, 1 TMA stores, 2 plain stores.
+    act     activation path of swap_ab tiles: 0 the library's choice, 1 TMA loads, 2
+            plain loads right after the dependency wait (M <= bm, one tile or cluster
+            segment per CTA, and all of that segment's k-blocks in the ring at once).
     """
 
     bm: int
@@ -72,6 +75,7 @@ class Config:
     ctas: int = 0
     cluster: int = 0
     store: int = 0
+    act: int = 0
 
     @property
     def swapped(self) -> bool:
@@ -84,6 +88,7 @@ class Config:
         tail += str(self.cluster) if self.split == 3 and self.cluster else ""
         tail += f" c{self.ctas}" if self.ctas else ""
         tail += {1: " tma", 2: " direct"}.get(self.store, "")
+        tail += {1: " act-tma", 2: " act-ld"}.get(self.act, "")
         return f"{self.bm}x{self.bn}x{self.bk} w{self.warps} s{self.stages} g{self.group_m}{tail}"
 
     def check(self) -> None:
@@ -97,8 +102,10 @@ class Config:
             raise NotSupported(f"{self.name}: tiles are bm 128 x bn in (128, 256)")
         if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1, 2, 3):
             raise NotSupported(f"{self.name}: bad stages/group_m/split")
-        if self.store not in (0, 1, 2):
-            raise NotSupported(f"{self.name}: store must be 0, 1 or 2")
+        if self.store not in (0, 1, 2) or self.act not in (0, 1, 2):
+            raise NotSupported(f"{self.name}: store and act must be 0, 1 or 2")
+        if self.act == 2 and not self.swapped:
+            raise NotSupported(f"{self.name}: direct activation loads take swap_ab tiles")
         if self.split == 3 and (not self.swapped or self.bm > 64 or not 0 <= self.cluster <= 8):
             raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles of <= 64 tokens")
 
@@ -106,7 +113,8 @@ class Config:
         return _native.I8LTile(
             swap_ab=1 if self.swapped else 0, tok_tile=self.bm if self.swapped else 128,
             w_tile=128 if self.swapped else self.bn, stages=self.stages, ctas=self.ctas,
-            group=self.group_m, split=self.split, cluster=self.cluster, store=self.store)
+            group=self.group_m, split=self.split, cluster=self.cluster, store=self.store,
+            act=self.act)
 
 
 def default_config(m: int, n: int, k: int) -> Config:

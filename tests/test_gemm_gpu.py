@@ -110,6 +110,40 @@ def test_decode_and_prefill_bf16_bit_exact(m, k, n):
     assert np.array_equal(bits(got), want)
 
 
+# (m, k, n, split, cluster): every token in one tile and each CTA's k-blocks in the ring.
+DIRECT_ACT = [(1, 2048, 4096, 3, 4), (1, 2048, 2048, 3, 8), (5, 1040, 1000, 3, 4),
+              (16, 2048, 4096, 3, 4), (17, 2048, 4096, 3, 4), (40, 256, 2048, 3, 2),
+              (64, 384, 4096, 3, 2), (1, 4096, 1024, 3, 8), (1, 512, 4096, 1, 0),
+              (3, 16, 300, 1, 0), (9, 272, 77, 3, 2)]
+
+
+@pytest.mark.parametrize("m,k,n,split,cluster", DIRECT_ACT)
+def test_direct_activation_loads_bit_exact(m, k, n, split, cluster):
+    """Activation k-blocks copied into shared memory by the epilogue warps (plain loads,
+    128-byte swizzle written by hand) give the same bits as the TMA path."""
+    a, w = ints((m, k), 90 + m), ints((n, k), 91)
+    g = torch.Generator().manual_seed(92)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    bm = default_config(m, n, k).bm
+    want_raw = exact(a, w)
+    want = to_bits(og.epilogue_f32(want_raw, np_(sa), np_(sb), np_(bias)), "bf16")
+    for act in (1, 2):
+        cfg = Config(bm, 128, swap_ab=True, split=split, cluster=cluster, act=act)
+        assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), want_raw), act
+        got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=cfg)
+        assert np.array_equal(bits(got), want), act
+
+
+def test_declines_direct_activation_loads_it_cannot_take():
+    a, w = ints((17, 2048), 1), ints((1024, 2048), 2)
+    with pytest.raises(NotSupported, match="direct activation"):   # two token tiles
+        w8a8_mm(a, w.t(), one(), one(), config=Config(16, 128, split=3, cluster=4, act=2))
+    with pytest.raises(NotSupported, match="direct activation"):   # 16 k-blocks per CTA
+        w8a8_mm(a[:1], w.t(), one(), one(), config=Config(16, 128, split=1, act=2))
+
+
 def test_declines_a_cluster_whose_partial_sums_do_not_fit():
     a, w = ints((64, 2048), 1), ints((1024, 2048), 2)
     with pytest.raises(NotSupported, match="ring"):
