@@ -352,12 +352,19 @@ def run_ours(args, world, rank, dev):
         e2e = run_e2e(layers, acts, cases, dev, world, max(1, min(args.steps, 5)))
 
     del graphs
-    standin = quant = standin_tp = None
+    standin = quant = standin_tp = standin_tp_peer = None
     if not args.no_standin and world == 1:
         standin = run_standin(dev)
         quant = run_quantisers(dev)
     if not args.no_standin and world > 1:
+        from int8_linear.tp import PeerComm
+
         standin_tp = run_standin_tp(dev, rank, world)
+        comm = PeerComm(device=dev)
+        try:
+            standin_tp_peer = run_standin_tp(dev, rank, world, comm)
+        finally:
+            comm.close()
 
     launches = args.steps * len(cases) * COPIES
     return {
@@ -365,6 +372,7 @@ def run_ours(args, world, rank, dev):
         "l2_warm_us": warm, "roofline": roofline, "roofline_other": other,
         "allgather_us_per_sweep": allgather_us, "e2e": e2e, "standin_us_per_layer": standin,
         "quantisers": quant, "standin_tp_us_per_layer": standin_tp,
+        "standin_tp_peer_us_per_layer": standin_tp_peer,
         "clocks": clocks.summary(), "gpu_launches": launches,
     }
 
@@ -418,9 +426,10 @@ def run_e2e(layers, acts, cases, dev, world, passes):
             "note": "one eager pass over the sweep through int8_linear.w8a8_mm, host copies included"}
 
 
-def run_standin_tp(dev, rank, world):
+def run_standin_tp(dev, rank, world, comm=None):
     """BASELINE config 4 under tensor parallelism: the stand-in decoder split over the
-    ranks (int8_linear/tp.py), µs per layer, max over ranks."""
+    ranks (int8_linear/tp.py), µs per layer, max over ranks.  With `comm` (a PeerComm)
+    the exchanges run in the library's NVLink kernels, else in NCCL collectives."""
     import torch
     import torch.distributed as dist
 
@@ -428,13 +437,15 @@ def run_standin_tp(dev, rank, world):
 
     out = {}
     for m in STANDIN_BATCHES:
-        s = TPStandinDecoder(m, rank, world, device=dev)
+        s = TPStandinDecoder(m, rank, world, device=dev, comm=comm)
         g = s.capture()
         dist.barrier()
         us = statistics.median([time_graph(g, windows=5) for _ in range(3)]) / LAYERS
         t = torch.tensor([us], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out[str(m)] = round(float(t.item()), 2)
+        torch.cuda.synchronize()
+        dist.barrier()
         del g, s
         torch.cuda.empty_cache()
     return out

@@ -247,6 +247,73 @@ int32_t i8l_get_pdl(void);
 /* Library version string and the compiled target, e.g. "0.1.0 sm_100a". */
 const char *i8l_version(void);
 
+/* ---- tensor parallelism over NVLink peer memory --------------------------------
+ * A row-parallel W8A8 layer (o_proj, down) leaves every GPU an int32 partial product;
+ * a row-split activation needs the global per-token absmax before it is quantised.
+ * These entry points do the exchange themselves, GPU to GPU over NVLink, fused with
+ * the computation that follows, in place of an NCCL collective plus a separate kernel.
+ * Every GPU owns one exchange buffer (i8l_peer_alloc) and opens every peer's buffer
+ * through its CUDA IPC handle (i8l_peer_open); the host exchanges the 64-byte handles
+ * (e.g. torch.distributed.all_gather_object).  All GPUs must make the same calls in
+ * the same order (SPMD); each call's waits for peers are bounded by timeout_ns, after
+ * which the status word (i8l_read_status) holds bit 64 and the outputs are invalid.
+ * No reference counterpart: the reference is single-GPU.
+ */
+#define I8L_MAX_RANKS 8
+#define I8L_PEER_HANDLE_BYTES 64
+
+typedef struct i8l_peer_comm {
+  void *bases[I8L_MAX_RANKS]; /* every GPU's exchange buffer, this GPU's at [rank]  */
+  uint32_t *epochs;           /* this GPU's call counters: max_rows zeroed uint32    */
+  int32_t rank, world;        /* world <= I8L_MAX_RANKS                              */
+  int64_t slot_bytes;         /* bytes per (parity, source) inbox slot, multiple of 16 */
+  int32_t max_rows;           /* rows per call (and epoch counters)                  */
+  uint64_t timeout_ns;        /* bound on each wait for a peer (0 = 2 s)             */
+} i8l_peer_comm;
+
+/* Bytes of one exchange buffer: 2 parities x world source slots (0 for a slot that is
+ * no positive multiple of 16 or a world outside [1, I8L_MAX_RANKS]).  Data travels as
+ * 8-byte words of {4-byte value, 4-byte call epoch}, so a row of N int32 takes 8*N
+ * bytes of a slot and a row's absmax 16 bytes. */
+size_t i8l_peer_buffer_bytes(int64_t slot_bytes, int32_t world);
+/* cudaMalloc + zero an exchange buffer on the current device; writes its IPC handle
+ * (I8L_PEER_HANDLE_BYTES) to handle_out. */
+int i8l_peer_alloc(size_t bytes, void **ptr, void *handle_out);
+/* Map a peer's exchange buffer from its IPC handle (peer access enabled lazily). */
+int i8l_peer_open(const void *handle, void **ptr);
+int i8l_peer_close(void *ptr);
+int i8l_peer_free(void *ptr);
+
+/* out[M,N] = cast(((float(sum over GPUs of partial) * sa) * sb) + bias): the one-GPU
+ * GEMM epilogue applied to the exact int32 sum.  N and ldp multiples of 4, N <= 8192,
+ * M*N*8 <= slot_bytes, M <= max_rows. */
+int i8l_tp_allreduce_dequant(const i8l_peer_comm *comm, const int32_t *partial, int64_t ldp,
+                             const float *sa, int32_t sa_per_row, const float *sb,
+                             int32_t sb_per_col, const void *bias, int32_t bias_dtype, void *out,
+                             int32_t out_dtype, int64_t ldo, int32_t M, int32_t N, void *stream);
+
+/* The same sum and dequant to the activation dtype (h, written to h_out if not NULL),
+ * then i8l_add_rmsnorm_quant(h, residual, weight) in the same pass: q, scale and
+ * residual_out equal the separate calls bit for bit.  N % 8 == 0. */
+int i8l_tp_allreduce_add_rmsnorm_quant(
+    const i8l_peer_comm *comm, const int32_t *partial, int64_t ldp, const float *sa,
+    int32_t sa_per_row, const float *sb, int32_t sb_per_col, const void *bias, int32_t bias_dtype,
+    const void *residual, int64_t ldr, const void *weight, int32_t act_dtype, int32_t w_dtype,
+    int8_t *q, int64_t ldq, float *scale, void *residual_out, int64_t ldro, void *h_out,
+    int64_t ldh, int32_t M, int32_t N, float eps, int32_t precise_div, void *stream);
+
+/* Per-token int8 of this GPU's column slice x[M, K] of rows split over the GPUs, with
+ * the scale of the whole row (absmax = MAX over the GPUs): every GPU's q slice and the
+ * (replicated) scale equal i8l_quant_rows on the whole row. */
+int i8l_tp_quant_rows(const i8l_peer_comm *comm, const void *x, int64_t ldx, int32_t act_dtype,
+                      int8_t *q, int64_t ldq, float *scale, int32_t M, int32_t K,
+                      int32_t precise_div, void *stream);
+
+/* The same for silu(gate)*up of this GPU's [gate_r | up_r] slice, [M, 2I] -> q [M, I]. */
+int i8l_tp_silu_mul_quant(const i8l_peer_comm *comm, const void *gate_up, int64_t ld,
+                          int32_t act_dtype, int8_t *q, int64_t ldq, float *scale, int32_t M,
+                          int32_t I, int32_t precise_div, int32_t round_silu, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -30,6 +30,18 @@ class I8LTile(ctypes.Structure):
         "act")]
 
 
+MAX_RANKS = 8
+PEER_HANDLE_BYTES = 64
+
+
+class I8LPeerComm(ctypes.Structure):
+    """Mirror of struct i8l_peer_comm."""
+
+    _fields_ = [("bases", ctypes.c_void_p * MAX_RANKS), ("epochs", ctypes.c_void_p),
+                ("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("slot_bytes", ctypes.c_int64),
+                ("max_rows", ctypes.c_int32), ("timeout_ns", ctypes.c_uint64)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -59,6 +71,21 @@ SIGNATURES = {
     "i8l_version": (ctypes.c_char_p, []),
     "i8l_set_pdl": (_i32, [_i32]),
     "i8l_get_pdl": (_i32, []),
+    "i8l_peer_buffer_bytes": (_sz, [_i64, _i32]),
+    "i8l_peer_alloc": (_i32, [_sz, ctypes.POINTER(_vp), _vp]),
+    "i8l_peer_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "i8l_peer_close": (_i32, [_vp]),
+    "i8l_peer_free": (_i32, [_vp]),
+    "i8l_tp_allreduce_dequant": (_i32, [ctypes.POINTER(I8LPeerComm), _vp, _i64, _fp, _i32, _fp, _i32,
+                                        _vp, _i32, _vp, _i32, _i64, _i32, _i32, _vp]),
+    "i8l_tp_allreduce_add_rmsnorm_quant": (_i32, [ctypes.POINTER(I8LPeerComm), _vp, _i64, _fp, _i32,
+                                                  _fp, _i32, _vp, _i32, _vp, _i64, _vp, _i32, _i32,
+                                                  _i8p, _i64, _fp, _vp, _i64, _vp, _i64, _i32, _i32,
+                                                  _f32, _i32, _vp]),
+    "i8l_tp_quant_rows": (_i32, [ctypes.POINTER(I8LPeerComm), _vp, _i64, _i32, _i8p, _i64, _fp, _i32,
+                                 _i32, _i32, _vp]),
+    "i8l_tp_silu_mul_quant": (_i32, [ctypes.POINTER(I8LPeerComm), _vp, _i64, _i32, _i8p, _i64, _fp,
+                                     _i32, _i32, _i32, _i32, _vp]),
 }
 
 

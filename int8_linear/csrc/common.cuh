@@ -22,6 +22,7 @@ enum StatusBits : int {
   kStatusDrainWait = 1 << 3,
   kStatusSelfTest = 1 << 4,
   kStatusClusterWait = 1 << 5,
+  kStatusPeerWait = 1 << 6,  // a tensor-parallel exchange waited too long for a peer GPU
 };
 
 // A wait that should take microseconds gives up after this many nanoseconds

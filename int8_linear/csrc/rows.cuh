@@ -1,0 +1,185 @@
+// Row helpers shared by the per-token quantisers (quant.cu) and the tensor-parallel
+// exchange kernels (peer.cu): block reductions, the vectorised row layout, the
+// reference's row quantiser and the launch shape of a one-row-per-CTA kernel.
+#pragma once
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace i8l {
+
+// Both reductions leave the result in every thread.  `red` holds 32 floats.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < nw ? red[l] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < nw ? red[l] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Which row elements thread t owns: vector v (0..NV-1) covers columns
+// [(v*blockDim + t)*VW, +VW).  VW is 8 (16-byte vectors of 16-bit values) or 1.
+template <int VW>
+__device__ __forceinline__ int col_of(int v) {
+  return (v * blockDim.x + threadIdx.x) * VW;
+}
+
+template <int DT, int VW>
+__device__ __forceinline__ void load_vec(const void *row, int col, float (&out)[VW]) {
+  using T = typename ActType<DT>::T;
+  const T *p = static_cast<const T *>(row) + col;
+  if constexpr (VW == 8 && sizeof(T) == 2) {
+    const uint4 raw = *reinterpret_cast<const uint4 *>(p);
+    const T *h = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = ActType<DT>::to_f32(h[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VW; ++i) out[i] = ActType<DT>::to_f32(p[i]);
+  }
+}
+
+template <int DT, int VW>
+__device__ __forceinline__ void store_vec(void *row, int col, const float (&in)[VW]) {
+  using T = typename ActType<DT>::T;
+  T *p = static_cast<T *>(row) + col;
+  if constexpr (VW == 8 && sizeof(T) == 2) {
+    uint4 raw;
+    T *h = reinterpret_cast<T *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = ActType<DT>::from_f32(in[i]);
+    *reinterpret_cast<uint4 *>(p) = raw;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VW; ++i) p[i] = ActType<DT>::from_f32(in[i]);
+  }
+}
+
+__device__ __forceinline__ float load_weight(const void *w, int dtype, int col) {
+  switch (dtype) {
+    case I8L_BF16:
+      return __bfloat162float(static_cast<const __nv_bfloat16 *>(w)[col]);
+    case I8L_F16:
+      return __half2float(static_cast<const __half *>(w)[col]);
+    default:
+      return static_cast<const float *>(w)[col];
+  }
+}
+
+// Rounds an fp32 value to the weight dtype and back (the reference's
+// xn.to(w.dtype)); fp32 weights leave it unchanged.
+__device__ __forceinline__ float round_to_weight(float v, int dtype) {
+  switch (dtype) {
+    case I8L_BF16:
+      return round_through<I8L_BF16>(v);
+    case I8L_F16:
+      return round_through<I8L_F16>(v);
+    default:
+      return v;
+  }
+}
+
+// The row quantiser of the reference (_quantize_row, fused_quant.py:41-53):
+// scale = absmax/127, inv = 127/absmax (0 for a zero row), q = rint(y*inv)
+// saturated to [-128, 127].  `y` holds this thread's values (0 where the thread
+// owns no column), `valid` marks the real ones.
+//
+// For rows split across GPUs: with amax_out the row's local absmax is written there and
+// nothing is quantised; with amax_in (e.g. the MAX over GPUs) that absmax is used in
+// place of the row's own, so every GPU quantises exactly as one GPU would.
+template <int NV, int VW>
+__device__ __forceinline__ void quantize_row(const float (&y)[NV][VW], int K, int8_t *qrow,
+                                             float *scale_out, int precise, float *red,
+                                             const float *amax_in = nullptr,
+                                             float *amax_out = nullptr) {
+  float amax = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int i = 0; i < VW; ++i) amax = fmaxf(amax, fabsf(y[v][i]));
+  amax = block_max(amax, red);
+  if (amax_out) {
+    if (threadIdx.x == 0) *amax_out = amax;
+    return;
+  }
+  if (amax_in) amax = *amax_in;
+  const float scale = precise ? div_rn(amax, 127.f) : div_full(amax, 127.f);
+  const float inv = amax == 0.f ? 0.f : (precise ? div_rn(127.f, amax) : div_full(127.f, amax));
+  if (threadIdx.x == 0) *scale_out = scale;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int col = col_of<VW>(v);
+    if (col >= K) continue;
+    int8_t q[VW];
+#pragma unroll
+    for (int i = 0; i < VW; ++i) {
+      int r = __float2int_rn(__fmul_rn(y[v][i], inv));
+      r = r < -128 ? -128 : (r > 127 ? 127 : r);
+      q[i] = static_cast<int8_t>(r);
+    }
+    if constexpr (VW == 8) {
+      *reinterpret_cast<uint2 *>(qrow + col) = *reinterpret_cast<const uint2 *>(q);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) qrow[col + i] = q[i];
+    }
+  }
+}
+
+// Threads and values per thread for a row of `cols` values: vectors of VW
+// values, the fewest vectors per thread that keep the CTA at <= 256 threads
+// (the scalar path may grow to 1024 threads of 16 values).
+struct RowShape {
+  int nv;
+  int threads;
+};
+
+inline bool row_shape(int cols, int vw, RowShape *s) {
+  const int vecs = (cols + vw - 1) / vw;
+  static const int kNv[] = {1, 2, 3, 4, 6, 8, 12, 16};
+  for (int nv : kNv) {
+    int threads = (vecs + nv - 1) / nv;
+    threads = ((threads + 31) / 32) * 32;
+    if (threads <= 256 || (vw == 1 && nv == 16 && threads <= 1024)) {
+      s->nv = nv;
+      s->threads = std::max(32, threads);
+      return true;
+    }
+  }
+  return false;
+}
+
+inline bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+#define I8L_DISPATCH_NV(NVVAL, ...)                                                \
+  switch (NVVAL) {                                                                 \
+    case 1: { constexpr int NV = 1; __VA_ARGS__; } break;                          \
+    case 2: { constexpr int NV = 2; __VA_ARGS__; } break;                          \
+    case 3: { constexpr int NV = 3; __VA_ARGS__; } break;                          \
+    case 4: { constexpr int NV = 4; __VA_ARGS__; } break;                          \
+    case 6: { constexpr int NV = 6; __VA_ARGS__; } break;                          \
+    case 8: { constexpr int NV = 8; __VA_ARGS__; } break;                          \
+    case 12: { constexpr int NV = 12; __VA_ARGS__; } break;                        \
+    default: { constexpr int NV = 16; __VA_ARGS__; } break;                        \
+  }
+
+}  // namespace i8l

@@ -107,10 +107,12 @@ class TPStandinDecoder:
     qkv and gate_up column-parallel (q, k, v and gate, up sharded separately), o_proj and
     down row-parallel with an exact int32 all-reduce, the row-split activations quantised
     with the global per-token absmax.  Built from the same seeded weights as
-    StandinDecoder, so every rank's output equals the one-GPU output bit for bit."""
+    StandinDecoder, so every rank's output equals the one-GPU output bit for bit.  With
+    `comm` (a tp.PeerComm) the exchanges run in this library's NVLink kernels, else in
+    NCCL collectives."""
 
     def __init__(self, m: int, rank: int, world: int, group=None, layers: int = LAYERS,
-                 seed: int = 0, device="cuda"):
+                 seed: int = 0, device="cuda", comm=None):
         from int8_linear import tp
 
         full = StandinDecoder(m, layers=layers, seed=seed, device=device)
@@ -132,10 +134,45 @@ class TPStandinDecoder:
             })
         del full
         torch.cuda.empty_cache()
+        self.comm = comm
         self.graph: torch.cuda.CUDAGraph | None = None
         self.out: torch.Tensor | None = None
 
     def step(self) -> torch.Tensor:
+        return self._step_peer() if self.comm is not None else self._step_nccl()
+
+    def _step_peer(self) -> torch.Tensor:
+        """The same step with the exchanges in this library's NVLink kernels: per layer
+        qkv GEMM -> split-row quantiser (absmax MAX over GPUs) -> o_proj partial GEMM ->
+        (int32 sum over GPUs + dequant + residual add + RMSNorm + quantiser) -> gate_up GEMM
+        -> split-row SiLU-mul quantiser -> down partial GEMM -> (sum + dequant + the next
+        layer's norm and quantiser).  Six kernels per layer instead of seven plus four
+        collectives."""
+        from int8_linear import tp
+
+        c = self.comm
+        res = self.x
+        q, s, _ = add_rmsnorm_quant(self.x, None, self.w, EPS)
+        q_cols = HIDDEN // self.world
+        h = None
+        last = len(self.layers) - 1
+        for i, layer in enumerate(self.layers):
+            qkv = layer["qkv"](q, s)
+            q, s = tp.peer_quant_rows(c, qkv[:, :q_cols])
+            acc = layer["o"].partial(q)
+            q, s, res = tp.peer_allreduce_add_rmsnorm_quant(c, acc, s, layer["o"].w_s, None, res,
+                                                            self.w, EPS)
+            gu = layer["gu"](q, s)
+            q, s = tp.peer_silu_mul_quant(c, gu)
+            acc = layer["dn"].partial(q)
+            if i < last:
+                q, s, res = tp.peer_allreduce_add_rmsnorm_quant(c, acc, s, layer["dn"].w_s, None, res,
+                                                                self.w, EPS)
+            else:
+                h = tp.peer_allreduce_dequant(c, acc, s, layer["dn"].w_s)
+        return h
+
+    def _step_nccl(self) -> torch.Tensor:
         from int8_linear import tp
 
         res = self.x
