@@ -571,15 +571,18 @@ def run_reference_triton_child(args):
     for name, k, n in layers_for(args.model):
         ws = [quant_rows_t((torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16))
               for _ in range(COPIES)]
+        bias = (torch.randn(n, generator=g, device=dev) * 0.01).to(torch.bfloat16)
         for m in M_SWEEP:
             a_q, a_s = quant_rows_t(torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16))
-            it = iter(range(1 << 40))
+            for b in (None, bias):    # the same 96 cases as our arm: with and without bias
+                it = iter(range(1 << 40))
 
-            def fn():
-                for _ in range(COPIES):
-                    wq, wsc = ws[next(it) % COPIES]
-                    ref_mm(a_q, wq.t(), a_s, wsc, torch.bfloat16)
-            per[f"{name}/{m}"] = round(time_graph(capture(fn)) / COPIES, 3)
+                def fn(b=b, it=it):
+                    for _ in range(COPIES):
+                        wq, wsc = ws[next(it) % COPIES]
+                        ref_mm(a_q, wq.t(), a_s, wsc, torch.bfloat16, b)
+                key = f"{name}/{m}" + ("" if b is None else "/bias")
+                per[key] = round(time_graph(capture(fn)) / COPIES, 3)
         del ws
     total = sum(per.values())
     try:
