@@ -41,6 +41,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "W8A8 GEMM µs & roofline % per (M,K,N); stand-in decode µs/layer at bs 1–128"
 M_SWEEP = [1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 1024, 4096]
+QUANT_M = [1, 16, 64, 128, 1024, 4096]    # BASELINE config 3 batch sizes timed
 STANDIN_BATCHES = [1, 2, 4, 8, 16, 32, 64, 128]
 COPIES = 8          # weight copies per layer = launches per shape per step (L2-cold)
 L2_BYTES = 126 << 20
@@ -453,16 +454,22 @@ def run_standin_tp(dev, rank, world, comm=None):
 
 def run_quantisers(dev):
     """the fused quantisers, µs per call (graph of 50 calls) and the
-    fraction of HBM bandwidth their algorithmic bytes reach."""
+    fraction of HBM bandwidth their algorithmic bytes reach.  Timed with the run's
+    programmatic-dependent-launch setting and, as `*_no_pdl`, without it: 50 identical
+    calls back to back are not what PDL is for (each call's CTAs start early beside
+    the previous call's on the same SMs); in a decode chain PDL overlaps each kernel
+    with the GEMM next to it."""
     import torch
 
+    from int8_linear import _native
     from int8_linear import fused_quant as fq
 
     pk = peaks()
     out = {}
+    pdl = _native.pdl_enabled()
     g = torch.Generator(device=dev).manual_seed(3)
     gamma = (1.0 + 0.1 * torch.randn(2048, generator=g, device=dev)).to(torch.bfloat16)
-    for m in (1, 16, 64, 128, 1024, 4096):
+    for m in QUANT_M:
         x = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
         r = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
         gu = torch.randn((m, 12288), generator=g, device=dev).to(torch.bfloat16)
@@ -470,10 +477,16 @@ def run_quantisers(dev):
         t_silu = time_graph(capture(lambda: [fq.silu_mul_quant(gu, True, True) for _ in range(50)])) / 50
         b_norm = m * (2048 * 7 + 4) + 2 * 2048
         b_silu = m * (6144 * 5 + 4)
+        _native.set_pdl(False)
+        t_norm0 = time_graph(capture(lambda: [fq.add_rmsnorm_quant(x, r, gamma, 1e-6) for _ in range(50)])) / 50
+        t_silu0 = time_graph(capture(lambda: [fq.silu_mul_quant(gu, True, True) for _ in range(50)])) / 50
+        _native.set_pdl(pdl)
         out[str(m)] = {"add_rmsnorm_quant_us": round(t_norm, 2),
                        "add_rmsnorm_quant_hbm_frac": round(b_norm / t_norm / 1e3 / pk["hbm_gbs"], 3),
                        "silu_mul_quant_us": round(t_silu, 2),
-                       "silu_mul_quant_hbm_frac": round(b_silu / t_silu / 1e3 / pk["hbm_gbs"], 3)}
+                       "silu_mul_quant_hbm_frac": round(b_silu / t_silu / 1e3 / pk["hbm_gbs"], 3),
+                       "add_rmsnorm_quant_us_no_pdl": round(t_norm0, 2),
+                       "silu_mul_quant_us_no_pdl": round(t_silu0, 2)}
     return out
 
 
@@ -601,6 +614,18 @@ def run_reference_triton_child(args):
             am = xf.abs().amax(-1, keepdim=True)
             inv = torch.where(am == 0, torch.zeros_like(am), 127.0 / am)
             return torch.round(xf * inv).clamp(-128, 127).to(torch.int8), am / 127.0
+    # BASELINE config 3 on the reference's Triton quantisers (same method as our arm:
+    # graph of 50 calls, µs per call)
+    quant = {}
+    for m in QUANT_M:
+        gq = torch.Generator(device=dev).manual_seed(3)
+        xq = torch.randn((m, 2048), generator=gq, device=dev).to(torch.bfloat16)
+        rq = torch.randn((m, 2048), generator=gq, device=dev).to(torch.bfloat16)
+        gam = (1 + 0.1 * torch.randn(2048, generator=gq, device=dev)).to(torch.bfloat16)
+        guq = torch.randn((m, 12288), generator=gq, device=dev).to(torch.bfloat16)
+        t_norm = time_graph(capture(lambda: [rfq.add_rmsnorm_quant(xq, rq, gam, 1e-6, True) for _ in range(50)])) / 50
+        t_silu = time_graph(capture(lambda: [rfq.silu_mul_quant(guq, True, True) for _ in range(50)])) / 50
+        quant[str(m)] = {"add_rmsnorm_quant_us": round(t_norm, 2), "silu_mul_quant_us": round(t_silu, 2)}
     standin = {}
     from int8_linear.shapes import SHAPES as RS  # noqa: F401  (the reference's own table)
     for m in STANDIN_BATCHES:
@@ -635,6 +660,7 @@ def run_reference_triton_child(args):
         del layers
         torch.cuda.empty_cache()
     print(json.dumps({"value": round(total, 2), "per_shape_us": per, "standin_us_per_layer": standin,
+                      "quantisers": quant,
                       "standin_o_proj_quantiser": qsrc, "triton": __import__("triton").__version__}))
 
 

@@ -246,6 +246,7 @@ struct ReduceNormArgs {
   long long ldh;
   float eps;
   int precise;
+  int w_vec;  // the norm weight pointer allows 16-byte loads
 };
 
 // Row thread layout of the norm kernel (add_rmsnorm_quant_kernel with VW = 8): thread t
@@ -254,10 +255,10 @@ struct ReduceNormArgs {
 // blockDim and NV as the norm kernel, the sum of squares is accumulated in the same
 // order, so the result equals dequant followed by add_rmsnorm_quant bit for bit.
 template <int DT, int NV>
-__global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(const ReduceNormArgs a) {
+__global__ void __launch_bounds__(row_max_threads(NV, 8)) tp_allreduce_norm_kernel(const ReduceNormArgs a) {
   using T = typename ActType<DT>::T;
   __shared__ unsigned s_e;
-  __shared__ float red[32];
+  __shared__ float red[32], red2[32];
   pdl_launch_dependents();
   pdl_wait();
   const ReduceArgs &ra = a.r;
@@ -297,11 +298,12 @@ __global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(const ReduceNorm
     }
     // 2. dequant to the activation dtype (the layer output h), + residual, RMSNorm
     const float sa = ra.sa_per_row ? ra.sa[row] : ra.sa[0];
-    float x[NV][8];
+    float x[NV][8], wv[NV][8];
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       const int c = col_of<8>(v);
       if (c < N) {
+        load_weight_vec<8>(a.w, a.w_dtype, c, a.w_vec != 0, wv[v]);
         const int q[8] = {acc[v][0].x, acc[v][0].y, acc[v][0].z, acc[v][0].w,
                           acc[v][1].x, acc[v][1].y, acc[v][1].z, acc[v][1].w};
 #pragma unroll
@@ -334,12 +336,12 @@ __global__ void __launch_bounds__(256) tp_allreduce_norm_kernel(const ReduceNorm
       for (int i = 0; i < 8; ++i) {
         if (c < N) {
           const float xn = round_to_weight(__fmul_rn(x[v][i], rs), a.w_dtype);
-          x[v][i] = round_through<DT>(__fmul_rn(xn, load_weight(a.w, a.w_dtype, c + i)));
+          x[v][i] = round_through<DT>(__fmul_rn(xn, wv[v][i]));
         }
       }
     }
-    quantize_row<NV, 8>(x, N, a.q + row * a.ldq, a.scale + row, a.precise, red);
-    __syncthreads();  // `red` is reused by the next row
+    quantize_row<NV, 8>(x, N, a.q + row * a.ldq, a.scale + row, a.precise, red2);
+    __syncthreads();  // `red` and `red2` are reused by the next row
   }
   peer_end(p, e);
 }
@@ -386,7 +388,7 @@ struct SplitQuantArgs {
 };
 
 template <int DT, int NV, int VW, bool kSilu>
-__global__ void __launch_bounds__(VW == 8 ? 256 : 1024) tp_split_quant_kernel(const SplitQuantArgs a) {
+__global__ void __launch_bounds__(row_max_threads(NV, VW)) tp_split_quant_kernel(const SplitQuantArgs a) {
   using T = typename ActType<DT>::T;
   __shared__ unsigned s_e;
   __shared__ float s_amax;
@@ -427,9 +429,11 @@ __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) tp_split_quant_kernel(co
 #pragma unroll
       for (int i = 0; i < VW; ++i) amax = fmaxf(amax, fabsf(y[v][i]));
     amax = block_max(amax, red);
-    global_absmax(a.p, row, e, amax, ok, &s_amax, s_part);
-    quantize_row<NV, VW>(y, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red, &s_amax);
-    __syncthreads();
+    const float m = global_absmax(a.p, row, e, amax, ok, &s_amax, s_part);
+    if (threadIdx.x == 0) a.scale[row] = a.precise ? div_rn(m, 127.f) : div_full(m, 127.f);
+    const float inv = m == 0.f ? 0.f : (a.precise ? div_rn(127.f, m) : div_full(127.f, m));
+    quantize_vals<NV, VW>(y, a.K, a.q + row * a.ldq, inv);
+    __syncthreads();  // `red`, `s_part` and `s_amax` are reused by the next row
   }
   peer_end(a.p, e);
 }
@@ -629,6 +633,7 @@ extern "C" int i8l_tp_allreduce_add_rmsnorm_quant(
   a.ldh = ldh;
   a.eps = eps;
   a.precise = precise_div;
+  a.w_vec = aligned16(weight) ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid(peer_grid(comm, M));
   const int nv = rs.nv, th = rs.threads;
@@ -666,7 +671,8 @@ static int split_quant(const i8l_peer_comm *comm, const void *x, int64_t ldx, in
   // The same thread layout as the one-GPU quantisers (so the code paths agree).
   const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldq % 8 == 0 && aligned16(x) && aligned16(q);
   RowShape rs;
-  if (!row_shape(K, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
+  if (!row_shape(K, vec ? 8 : 1, &rs, row_threads(M)))
+    return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid(peer_grid(comm, M));
   const int nv = rs.nv, th = rs.threads;

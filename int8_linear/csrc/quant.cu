@@ -38,22 +38,29 @@ struct NormArgs {
   int K;
   float eps;
   int precise;
+  int w_vec;  // the weight pointer allows 16-byte loads
 };
 
-template <int DT, int NV, int VW>
-__global__ void __launch_bounds__(VW == 8 ? 256 : 1024) add_rmsnorm_quant_kernel(const NormArgs a) {
+// WDT: the weight dtype fixed at compile time (vector rows), or -1 to read it from the
+// arguments (scalar rows).
+template <int DT, int NV, int VW, int WDT>
+__global__ void __launch_bounds__(row_max_threads(NV, VW)) add_rmsnorm_quant_kernel(const NormArgs a) {
+  const int wdt = WDT >= 0 ? WDT : a.w_dtype;
+  // Let the next kernel in the stream start its prologue now (in a decode chain, the
+  // next GEMM prefetches its weights while this row is normalised).
   pdl_launch_dependents();
   pdl_wait();
-  __shared__ float red[32];
+  __shared__ float red[32], red2[32];
   using T = typename ActType<DT>::T;
   const long long row = blockIdx.x;
   const T *xrow = static_cast<const T *>(a.x) + row * a.ldx;
-  float x[NV][VW];
+  float x[NV][VW], wv[NV][VW];
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
     const int col = col_of<VW>(v);
     if (col < a.K) {
       load_vec<DT, VW>(xrow, col, x[v]);
+      load_weight_vec<VW>(a.w, wdt, col, a.w_vec != 0, wv[v]);
       if (a.res) {
         float r[VW];
         load_vec<DT, VW>(static_cast<const T *>(a.res) + row * a.ldr, col, r);
@@ -81,13 +88,12 @@ __global__ void __launch_bounds__(VW == 8 ? 256 : 1024) add_rmsnorm_quant_kernel
 #pragma unroll
     for (int i = 0; i < VW; ++i) {
       if (col < a.K) {
-        const float xn = round_to_weight(__fmul_rn(x[v][i], rs), a.w_dtype);
-        const float wv = load_weight(a.w, a.w_dtype, col + i);
-        x[v][i] = round_through<DT>(__fmul_rn(xn, wv));
+        const float xn = round_to_weight(__fmul_rn(x[v][i], rs), wdt);
+        x[v][i] = round_through<DT>(__fmul_rn(xn, wv[v][i]));
       }
     }
   }
-  quantize_row<NV, VW>(x, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red);
+  quantize_row<NV, VW>(x, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red2);
 }
 
 struct SiluArgs {
@@ -104,7 +110,7 @@ struct SiluArgs {
 };
 
 template <int DT, int NV, int VW>
-__global__ void __launch_bounds__(VW == 8 ? 256 : 1024) silu_mul_quant_kernel(const SiluArgs a) {
+__global__ void __launch_bounds__(row_max_threads(NV, VW)) silu_mul_quant_kernel(const SiluArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[32];
@@ -149,7 +155,7 @@ struct QuantArgs {
 };
 
 template <int DT, int NV, int VW>
-__global__ void __launch_bounds__(VW == 8 ? 256 : 1024) quant_rows_kernel(const QuantArgs a) {
+__global__ void __launch_bounds__(row_max_threads(NV, VW)) quant_rows_kernel(const QuantArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[32];
@@ -257,7 +263,8 @@ extern "C" int i8l_add_rmsnorm_quant(const void *x, int64_t ldx, const void *res
     return set_error(I8L_EINVAL, "residual and residual_out must be given together");
   if (ldx < K || ldq < K || (residual && (ldr < K || ldro < K)))
     return set_error(I8L_EINVAL, "row stride smaller than K");
-  NormArgs a{x, ldx, residual, ldr, weight, w_dtype, q, ldq, scale, rout, ldro, K, eps, precise_div};
+  NormArgs a{x, ldx, residual, ldr, weight, w_dtype, q, ldq, scale, rout, ldro, K, eps, precise_div,
+             aligned16(weight) ? 1 : 0};
   const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldq % 8 == 0 && aligned16(x) && aligned16(q) &&
                    (!residual || (ldr % 8 == 0 && ldro % 8 == 0 && aligned16(residual) &&
                                   aligned16(rout)));
@@ -266,19 +273,26 @@ extern "C" int i8l_add_rmsnorm_quant(const void *x, int64_t ldx, const void *res
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nv = rs.nv, th = rs.threads;
   cudaError_t err = cudaSuccess;
+#define I8L_NORM_VEC(ADT, WDTV) \
+  I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<ADT, NV, 8, WDTV>, dim3(M), dim3(th), 0, s, 1, a)))
   if (act_dtype == I8L_BF16) {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_BF16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
+      if (w_dtype == I8L_BF16) { I8L_NORM_VEC(I8L_BF16, I8L_BF16) }
+      else if (w_dtype == I8L_F16) { I8L_NORM_VEC(I8L_BF16, I8L_F16) }
+      else { I8L_NORM_VEC(I8L_BF16, I8L_F32) }
     } else {
-      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_BF16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
+      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_BF16, NV, 1, -1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   } else {
     if (vec) {
-      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_F16, NV, 8>, dim3(M), dim3(th), 0, s, 1, a)))
+      if (w_dtype == I8L_BF16) { I8L_NORM_VEC(I8L_F16, I8L_BF16) }
+      else if (w_dtype == I8L_F16) { I8L_NORM_VEC(I8L_F16, I8L_F16) }
+      else { I8L_NORM_VEC(I8L_F16, I8L_F32) }
     } else {
-      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_F16, NV, 1>, dim3(M), dim3(th), 0, s, 1, a)))
+      I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<I8L_F16, NV, 1, -1>, dim3(M), dim3(th), 0, s, 1, a)))
     }
   }
+#undef I8L_NORM_VEC
   return finish_launch(err, "add_rmsnorm_quant launch");
 }
 
@@ -305,7 +319,7 @@ extern "C" int i8l_silu_mul_quant_ex(const void *gate_up, int64_t ld, int32_t ac
   const bool vec = I % 8 == 0 && ld % 8 == 0 && aligned16(gate_up) &&
                    (absmax_out || (ldq % 8 == 0 && aligned16(q)));
   RowShape rs;
-  if (!row_shape(I, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", I);
+  if (!row_shape(I, vec ? 8 : 1, &rs, row_threads(M))) return set_error(I8L_ENOTSUP, "row of %d values is too long", I);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nv = rs.nv, th = rs.threads;
   cudaError_t err = cudaSuccess;
@@ -347,7 +361,7 @@ extern "C" int i8l_quant_rows_ex(const void *x, int64_t ldx, int32_t act_dtype, 
   const bool vec = K % 8 == 0 && ldx % 8 == 0 && aligned16(x) &&
                    (absmax_out || (ldq % 8 == 0 && aligned16(q)));
   RowShape rs;
-  if (!row_shape(K, vec ? 8 : 1, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
+  if (!row_shape(K, vec ? 8 : 1, &rs, row_threads(M))) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nv = rs.nv, th = rs.threads;
   cudaError_t err = cudaSuccess;

@@ -6,15 +6,17 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace i8l {
 
-// Both reductions leave the result in every thread.  `red` holds 32 floats.
+// Both reductions leave the result in every thread.  `red` holds 32 floats that no
+// thread reads or writes between the previous barrier and this call (each reduction of
+// a row gets its own array; a loop over rows ends each row with a barrier).
 __device__ __forceinline__ float block_sum(float v, float *red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();
   if (l == 0) red[w] = v;
   __syncthreads();
   v = l < nw ? red[l] : 0.f;
@@ -27,7 +29,6 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();
   if (l == 0) red[w] = v;
   __syncthreads();
   v = l < nw ? red[l] : 0.f;
@@ -74,6 +75,39 @@ __device__ __forceinline__ void store_vec(void *row, int col, const float (&in)[
   }
 }
 
+__device__ __forceinline__ float load_weight(const void *w, int dtype, int col);
+
+// VW consecutive weight values from column col: one 16-byte load (two for fp32) when
+// `vec` (the weight pointer is 16-byte aligned and VW == 8), else scalar loads.
+template <int VW>
+__device__ __forceinline__ void load_weight_vec(const void *w, int dtype, int col, bool vec,
+                                                float (&out)[VW]) {
+  if constexpr (VW == 8) {
+    if (vec && (dtype == I8L_BF16 || dtype == I8L_F16)) {
+      const uint4 raw = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(w) + col);
+      if (dtype == I8L_BF16) {
+        const __nv_bfloat16 *h = reinterpret_cast<const __nv_bfloat16 *>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = __bfloat162float(h[i]);
+      } else {
+        const __half *h = reinterpret_cast<const __half *>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = __half2float(h[i]);
+      }
+      return;
+    }
+    if (vec && dtype == I8L_F32) {
+      const float4 a = *reinterpret_cast<const float4 *>(static_cast<const float *>(w) + col);
+      const float4 b = *reinterpret_cast<const float4 *>(static_cast<const float *>(w) + col + 4);
+      out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+      out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VW; ++i) out[i] = load_weight(w, dtype, col + i);
+}
+
 __device__ __forceinline__ float load_weight(const void *w, int dtype, int col) {
   switch (dtype) {
     case I8L_BF16:
@@ -95,6 +129,30 @@ __device__ __forceinline__ float round_to_weight(float v, int dtype) {
       return round_through<I8L_F16>(v);
     default:
       return v;
+  }
+}
+
+// q = rint(y * inv) saturated to [-128, 127] for this thread's values in columns < K
+// of `qrow` (the quantising half of quantize_row, for an absmax found elsewhere).
+template <int NV, int VW>
+__device__ __forceinline__ void quantize_vals(const float (&y)[NV][VW], int K, int8_t *qrow, float inv) {
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int col = col_of<VW>(v);
+    if (col >= K) continue;
+    int8_t q[VW];
+#pragma unroll
+    for (int i = 0; i < VW; ++i) {
+      int r = __float2int_rn(__fmul_rn(y[v][i], inv));
+      r = r < -128 ? -128 : (r > 127 ? 127 : r);
+      q[i] = static_cast<int8_t>(r);
+    }
+    if constexpr (VW == 8) {
+      *reinterpret_cast<uint2 *>(qrow + col) = *reinterpret_cast<const uint2 *>(q);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) qrow[col + i] = q[i];
+    }
   }
 }
 
@@ -122,27 +180,16 @@ __device__ __forceinline__ void quantize_row(const float (&y)[NV][VW], int K, in
     return;
   }
   if (amax_in) amax = *amax_in;
-  const float scale = precise ? div_rn(amax, 127.f) : div_full(amax, 127.f);
+  if (threadIdx.x == 0) *scale_out = precise ? div_rn(amax, 127.f) : div_full(amax, 127.f);
   const float inv = amax == 0.f ? 0.f : (precise ? div_rn(127.f, amax) : div_full(127.f, amax));
-  if (threadIdx.x == 0) *scale_out = scale;
-#pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int col = col_of<VW>(v);
-    if (col >= K) continue;
-    int8_t q[VW];
-#pragma unroll
-    for (int i = 0; i < VW; ++i) {
-      int r = __float2int_rn(__fmul_rn(y[v][i], inv));
-      r = r < -128 ? -128 : (r > 127 ? 127 : r);
-      q[i] = static_cast<int8_t>(r);
-    }
-    if constexpr (VW == 8) {
-      *reinterpret_cast<uint2 *>(qrow + col) = *reinterpret_cast<const uint2 *>(q);
-    } else {
-#pragma unroll
-      for (int i = 0; i < VW; ++i) qrow[col + i] = q[i];
-    }
-  }
+  quantize_vals<NV, VW>(y, K, qrow, inv);
+}
+
+// Most threads a one-row CTA may have with NV vectors of VW values per thread (the
+// kernels' launch bounds): 1024 for one or two vectors per thread or scalar rows,
+// else 256.
+constexpr __host__ __device__ int row_max_threads(int nv, int vw) {
+  return (vw == 1 || nv <= 2) ? 1024 : 256;
 }
 
 // Threads and values per thread for a row of `cols` values: vectors of VW
@@ -153,19 +200,35 @@ struct RowShape {
   int threads;
 };
 
-inline bool row_shape(int cols, int vw, RowShape *s) {
+// `max_threads` above 256 spreads a row thinner (fewer values per thread, shorter
+// chains of loads and math per thread), which pays for batches with fewer rows than
+// SMs; with many rows per SM, 256 threads with more values each keep more work in
+// flight.  Only kernels whose row reduction is a maximum may pick the shape per call
+// (row_threads); a sum of squares keeps one shape, so that a row's result does not
+// depend on the batch it came in.
+inline bool row_shape(int cols, int vw, RowShape *s, int max_threads = 256) {
   const int vecs = (cols + vw - 1) / vw;
   static const int kNv[] = {1, 2, 3, 4, 6, 8, 12, 16};
   for (int nv : kNv) {
     int threads = (vecs + nv - 1) / nv;
     threads = ((threads + 31) / 32) * 32;
-    if (threads <= 256 || (vw == 1 && nv == 16 && threads <= 1024)) {
+    const int cap = std::min(max_threads > 256 ? max_threads : (vw == 1 && nv == 16 ? 1024 : 256),
+                             row_max_threads(nv, vw));
+    if (threads <= cap) {
       s->nv = nv;
       s->threads = std::max(32, threads);
       return true;
     }
   }
   return false;
+}
+
+// Row-shape thread cap for a max-reduction row kernel over a batch of M rows: up to
+// 1024 threads while there are fewer rows than SMs, 256 beyond.
+inline int row_threads(int M) {
+  DeviceInfo di;
+  const int sms = device_info(&di) == I8L_OK ? di.sms : 148;
+  return M < sms ? 1024 : 256;
 }
 
 inline bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }

@@ -164,3 +164,29 @@ def test_split_row_quantisation_with_a_given_absmax(m, k):
 
 def np_t(x):
     return x.float()
+
+
+@pytest.mark.parametrize("kind", ["silu", "plain"])
+@pytest.mark.parametrize("m,cols", [(1, 6144), (5, 6144), (3, 14336), (17, 4096), (9, 3080), (2, 12296)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_batch_rows_equal_large_batch_rows(kind, m, cols, dtype):
+    """A decode batch (fewer rows than SMs) spreads each row over up to 1024 threads; the
+    same rows inside a batch of 200 use 256-thread CTAs.  The row reduction is a maximum,
+    so both give the same bits."""
+    g = torch.Generator().manual_seed(m * 13 + cols)
+    width = 2 * cols if kind == "silu" else cols
+    big = (torch.randn((200, width), generator=g) * 3).to(dtype).cuda()
+    small = big[:m].contiguous()
+    if kind == "silu":
+        for rs in (False, True):
+            q0, s0 = fq.silu_mul_quant(big, True, rs)
+            q1, s1 = fq.silu_mul_quant(small, True, rs)
+            assert torch.equal(q1, q0[:m]) and torch.equal(s1, s0[:m])
+    else:
+        q0, s0 = fq.per_token_quant(big)
+        q1, s1 = fq.per_token_quant(small)
+        assert torch.equal(q1, q0[:m]) and torch.equal(s1, s0[:m])
+        xs = big[:m, 4:cols - 4]           # an unaligned slice takes the scalar path
+        q2, s2 = fq.per_token_quant(xs)
+        qo, so = oq.quant_ieee(np_(xs))
+        check(q2, s2, qo, so, exact=True)
