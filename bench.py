@@ -276,11 +276,13 @@ def run_ours(args, world, rank, dev):
         if world > 1:
             dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed_region")   # `ncu --nvtx --nvtx-include timed_region/`
         t0.record(stream)
         for _ in range(args.steps):
             for g in graphs:
                 g.replay()
         t1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
