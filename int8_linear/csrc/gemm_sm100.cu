@@ -73,6 +73,10 @@ struct GemmArgs {
   int act_direct;
   const int8_t *act;
   long long lda;
+  // CTA pairs (cta_group::2): the two CTAs of each 2-CTA cluster compute one tile of
+  // 256 X rows (tiles_x counts 256-row tiles) x TN Y rows; each loads 128 X rows and
+  // TN/2 Y rows per k-block, the even CTA issues the 256-row MMAs.  Whole tiles only.
+  int pair;
 };
 
 struct Segment {
@@ -90,6 +94,11 @@ struct Schedule {
   // (64-bit ones for stream-K) then overlap the previous kernel instead of delaying
   // the first load after the wait.
   __device__ __forceinline__ void init(const GemmArgs &a) {
+    if (a.pair) {  // both CTAs of a pair walk the same tiles
+      dp_next = static_cast<int>(blockIdx.x) >> 1;
+      it = it_end = 0;
+      return;
+    }
     if (a.cluster > 1) {
       // One tile per cluster; CTA rank r takes the r-th of `cluster` equal k ranges.
       const int r = static_cast<int>(blockIdx.x) % a.cluster;
@@ -109,6 +118,14 @@ struct Schedule {
   }
 
   __device__ __forceinline__ bool next(const GemmArgs &a, Segment &s) {
+    if (a.pair) {
+      if (dp_next >= a.total_tiles) return false;
+      s.tile = dp_next;
+      s.kb0 = 0;
+      s.kb1 = a.kblocks;
+      dp_next += static_cast<int>(gridDim.x) >> 1;
+      return true;
+    }
     if (a.cluster > 1) {
       if (dp_next < 0) return false;
       s.tile = dp_next;
@@ -167,6 +184,13 @@ __device__ __forceinline__ void tile_coords(const GemmArgs &a, int t, int &tx,
   const int r = t - g * per_group;
   tx = first + r % gsz;
   ty = r / gsz;
+}
+
+// This CTA's (x tile, y tile): with CTA pairs the 256-row x tile of the pair is split
+// into the two CTAs' 128-row halves.
+__device__ __forceinline__ void cta_tile(const GemmArgs &a, int t, int &tx, int &ty) {
+  tile_coords(a, t, tx, ty);
+  if (a.pair) tx = 2 * tx + static_cast<int>(blockIdx.x & 1u);
 }
 
 __device__ __forceinline__ float load_scalar_f(const void *p, int dtype, long long i) {
@@ -298,9 +322,10 @@ constexpr int kStagingBytes = kEpiWarps * 2 * kStageBufBytes;   // 16 KB
 constexpr int kScalFloats = 256;                                // per array per buffer
 constexpr int kScalBytes = 2 * 2 * kScalFloats * 4;             // [2 arrays][2 acc][256]
 
-template <int TN>
+template <int TN, bool kPair = false>
 struct SmemLayout {
-  static constexpr int kYBytes = TN * kBK;
+  static constexpr int kYRows = kPair ? TN / 2 : TN;  // Y rows this CTA holds per stage
+  static constexpr int kYBytes = kYRows * kBK;
   static constexpr int kStageBytes = kXBytes + kYBytes;
   // Decode tiles rotate their k-steps over several accumulators: a chain of
   // accumulating MMAs into the same columns runs one MMA at a time, and an N=16 MMA
@@ -475,13 +500,16 @@ __device__ __forceinline__ void load_act_direct(const GemmArgs &a, uint8_t *sy, 
 
 // Decode tiles (TN <= 64) cap registers so two CTAs fit on an SM: with programmatic
 // dependent launch the next GEMM's CTA streams its weights beside this one.
-template <int TN>
+template <int TN, bool kPair>
 __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     w8a8_gemm_sm100(const __grid_constant__ CUtensorMap map_x,
                     const __grid_constant__ CUtensorMap map_y,
                     const __grid_constant__ CUtensorMap map_out,
                     const __grid_constant__ CUtensorMap map_ws, const GemmArgs a) {
-  using L = SmemLayout<TN>;
+  using L = SmemLayout<TN, kPair>;
+  // CTA pairs: rank 1 loads its halves and runs its epilogue; rank 0 also issues the MMAs.
+  const int rank = kPair ? static_cast<int>(blockIdx.x & 1u) : 0;
+  const bool leader = rank == 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -512,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpiWarps);
+      mbar_init(&acc_empty[i], kPair ? 2 * kEpiWarps : kEpiWarps);  // both CTAs' epilogues
     }
     mbar_init(drain, 1);
     mbar_init(peer_bar, 1);
@@ -539,15 +567,21 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     if (a.sk_iters > 0) tma_prefetch_desc(&map_ws);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, L::kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, L::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, L::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Every CTA's barriers are initialised before any CTA of the cluster signals them.
-  if (a.cluster > 1) cluster_sync();
+  // Every CTA's barriers (and a pair's TMEM) are set up before any CTA of the cluster
+  // signals them.
+  if (a.cluster > 1 || kPair) cluster_sync();
   // The next kernel in the stream may start its own prologue now; it waits for this
   // grid before touching anything this grid writes.
   pdl_launch_dependents();
@@ -557,6 +591,29 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     if (lane == 0) {
       const uint64_t pol_x = a.swap ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_y = policy_evict_last();
+      // One X / Y tile of a stage.  CTA pairs: this CTA's 128 X rows and its half of the
+      // TN Y rows, counted on the even CTA's `full` barrier.
+      auto load_x = [&](int st, int kb, int tx) {
+        if constexpr (kPair)
+          tma_load_2d_pair(sx + static_cast<size_t>(st) * kXBytes, &map_x,
+                           map_to_rank(smem_u32(&full[st]), 0), kb * kBK, tx * kXRows, pol_x);
+        else
+          tma_load_2d(sx + static_cast<size_t>(st) * kXBytes, &map_x, &full[st], kb * kBK,
+                      tx * kXRows, pol_x);
+      };
+      auto load_y = [&](int st, int kb, int ty) {
+        if constexpr (kPair)
+          tma_load_2d_pair(sy + static_cast<size_t>(st) * L::kYBytes, &map_y,
+                           map_to_rank(smem_u32(&full[st]), 0), kb * kBK,
+                           ty * TN + rank * L::kYRows, pol_y);
+        else
+          tma_load_2d(sy + static_cast<size_t>(st) * L::kYBytes, &map_y, &full[st], kb * kBK,
+                      ty * TN, pol_y);
+      };
+      // Bytes one stage's `full` barrier waits for (both CTAs' with pairs; armed by the
+      // even CTA only).
+      const uint32_t stage_tx = kPair ? 2u * L::kStageBytes
+                                      : (a.act_direct ? static_cast<uint32_t>(kXBytes) : L::kStageBytes);
       // Weight tiles of the first stages are loaded before waiting for the previous
       // kernel: inference weights are never written by the kernel just before.  The
       // weight is X with swap_ab, else Y.  Activations wait for pdl_wait().
@@ -567,15 +624,13 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
         Segment sg;
         while (pre < S && ps.next(a, sg)) {
           int tx, ty;
-          tile_coords(a, sg.tile, tx, ty);
+          cta_tile(a, sg.tile, tx, ty);
           for (int kb = sg.kb0; kb < sg.kb1 && pre < S; ++kb, ++pre) {
-            mbar_arrive_expect_tx(&full[pre], a.act_direct ? kXBytes : L::kStageBytes);
+            if (leader) mbar_arrive_expect_tx(&full[pre], stage_tx);
             if (a.swap)
-              tma_load_2d(sx + static_cast<size_t>(pre) * kXBytes, &map_x, &full[pre], kb * kBK,
-                          tx * kXRows, pol_x);
+              load_x(pre, kb, tx);
             else
-              tma_load_2d(sy + static_cast<size_t>(pre) * L::kYBytes, &map_y, &full[pre],
-                          kb * kBK, ty * TN, pol_y);
+              load_y(pre, kb, ty);
           }
         }
       }
@@ -589,29 +644,25 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
       bool ok = true;
       while (ok && sch.next(a, seg)) {
         int tx, ty;
-        tile_coords(a, seg.tile, tx, ty);
+        cta_tile(a, seg.tile, tx, ty);
         for (int kb = seg.kb0; kb < seg.kb1; ++kb) {
           if (issued < pre) {
             // Stage already claimed above with its weight tile: add the activation
             // (with direct activation loads the epilogue warps fill the Y slot).
             if (a.act_direct) {
             } else if (a.swap)
-              tma_load_2d(sy + static_cast<size_t>(stage) * L::kYBytes, &map_y, &full[stage],
-                          kb * kBK, ty * TN, pol_y);
+              load_y(stage, kb, ty);
             else
-              tma_load_2d(sx + static_cast<size_t>(stage) * kXBytes, &map_x, &full[stage],
-                          kb * kBK, tx * kXRows, pol_x);
+              load_x(stage, kb, tx);
           } else {
             if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, a.status,
                                    kStatusProducerWait)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-            tma_load_2d(sx + static_cast<size_t>(stage) * kXBytes, &map_x, &full[stage],
-                        kb * kBK, tx * kXRows, pol_x);
-            tma_load_2d(sy + static_cast<size_t>(stage) * L::kYBytes, &map_y, &full[stage],
-                        kb * kBK, ty * TN, pol_y);
+            if (leader) mbar_arrive_expect_tx(&full[stage], kPair ? stage_tx : L::kStageBytes);
+            load_x(stage, kb, tx);
+            load_y(stage, kb, ty);
           }
           ++issued;
           if (++stage == S) {
@@ -620,8 +671,10 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           }
         }
       }
-      if (!ok) {
-        // Let the loads already issued land before the CTA exits.
+      if (!ok && leader) {
+        // Let the loads already issued land before the CTA exits (a pair's loads are
+        // all counted on the even CTA's barriers; the odd CTA stays alive until the
+        // even one leaves, at the cluster barrier at the end).
         int st = stage;
         uint32_t ph = phase;
         const long long n = issued < S ? issued : S;
@@ -637,8 +690,9 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_i8(kXRows, TN);
+    // (CTA pairs: the even CTA issues the 256-row MMAs for both.)
+    if (lane == 0 && leader) {
+      constexpr uint32_t kIdesc = idesc_i8(kPair ? 2 * kXRows : kXRows, TN);
       Schedule sch;
       sch.init(a);
       Segment seg;
@@ -674,18 +728,28 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k, ++kstep) {
             const int ch = kstep % L::kChains;
-            mma_i8(d + static_cast<uint32_t>(ch * TN), ad + 2 * k, bd + 2 * k, kIdesc,
-                   kstep >= L::kChains ? 1u : 0u);
+            if constexpr (kPair)
+              mma_i8_pair(d + static_cast<uint32_t>(ch * TN), ad + 2 * k, bd + 2 * k, kIdesc,
+                          kstep >= L::kChains ? 1u : 0u);
+            else
+              mma_i8(d + static_cast<uint32_t>(ch * TN), ad + 2 * k, bd + 2 * k, kIdesc,
+                     kstep >= L::kChains ? 1u : 0u);
           }
           issued_any = true;
-          mma_commit(&empty[stage]);
+          if constexpr (kPair)
+            mma_commit_pair_mc(&empty[stage], 0x3);  // frees the stage in both CTAs
+          else
+            mma_commit(&empty[stage]);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&acc_full[acc]);
+        if constexpr (kPair)
+          mma_commit_pair_mc(&acc_full[acc], 0x3);  // both CTAs' epilogues may read
+        else
+          mma_commit(&acc_full[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -693,7 +757,10 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
       }
       if (!ok && issued_any) {
         // Let the MMAs in flight finish before TMEM and shared memory go away.
-        mma_commit(drain);
+        if constexpr (kPair)
+          mma_commit_pair(drain);
+        else
+          mma_commit(drain);
         volatile int no_abort = 0;
         mbar_wait_bounded(drain, 0, &no_abort, a.status, kStatusDrainWait);
       }
@@ -703,6 +770,18 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const int epi_tid = threadIdx.x - 64;
+    // This warp is done reading an accumulator (CTA pairs: the even CTA's barrier
+    // counts both CTAs' epilogue warps).
+    auto release_acc = [&](uint64_t *bar) {
+      if constexpr (kPair) {
+        if (leader)
+          mbar_arrive(bar);
+        else
+          mbar_arrive_remote(map_to_rank(smem_u32(bar), 0));
+      } else {
+        mbar_arrive(bar);
+      }
+    };
     Schedule sch;
     sch.init(a);
     Segment seg;
@@ -723,7 +802,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     uint32_t acc_phase = 0;
     while (sch.next(a, seg)) {
       TileCtx t;
-      tile_coords(a, seg.tile, t.tx, t.ty);
+      cta_tile(a, seg.tile, t.tx, t.ty);
       t.ncols = live_cols<TN>(a, t.ty);
       t.taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                 static_cast<uint32_t>(acc * L::kAccCols);
@@ -793,7 +872,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          if (lane == 0) release_acc(&acc_empty[acc]);
         } else {
           if (epi_tid == 0 && !a.cluster_early) {
             mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * kXRows * 4));
@@ -808,7 +887,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
             if (c0 + 16 >= t.ncols) {
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+              if (lane == 0) release_acc(&acc_empty[acc]);
             }
             if (!got) continue;
             for (int p = 1; p < a.cluster; ++p) {
@@ -838,7 +917,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          if (lane == 0) release_acc(&acc_empty[acc]);
         } else if (a.swap) {
           for (int c0 = 0; c0 < t.ncols; c0 += 16) {
             uint32_t r[16];
@@ -846,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
             if (c0 + 16 >= t.ncols) {
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+              if (lane == 0) release_acc(&acc_empty[acc]);
             }
             emit_swap16<TN>(a, &map_out, t, quarter, lane, c0, r, st);
           }
@@ -859,7 +938,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
             if (c0 + step >= t.ncols) {
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+              if (lane == 0) release_acc(&acc_empty[acc]);
             }
             emit_normal<TN>(a, &map_out, t, quarter, lane, c0, r0, r1, st);
           }
@@ -874,7 +953,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           if (c0 + 16 >= t.ncols) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            if (lane == 0) release_acc(&acc_empty[acc]);
           }
           uint8_t *buf = st.acquire(lane);
           uint32_t *b32 = reinterpret_cast<uint32_t *>(buf);
@@ -941,9 +1020,15 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
 
   tc_fence_before();
   __syncthreads();
+  // A pair's CTAs leave together: neither exits while the other may still signal its
+  // barriers or the even CTA's MMAs may still read its shared memory.
+  if constexpr (kPair) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::kTmemCols);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem_base, L::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, L::kTmemCols);
   }
 }
 
@@ -1014,8 +1099,9 @@ static size_t smem_extra() { return 1024 + kStagingBytes + kScalBytes + 8 * 8 + 
 // Shared memory of one of two CTAs that share an SM (228 KB minus 1 KB reserved per CTA).
 constexpr int kHalfSmem = 233472 / 2 - 1024;
 
-static int max_stages_for(int tn, int smem_optin) {
-  const int stage = kXBytes + tn * kBK;
+// `y_rows`: Y rows one CTA holds per stage (TN, or TN/2 for a CTA pair).
+static int max_stages_for(int y_rows, int smem_optin) {
+  const int stage = kXBytes + y_rows * kBK;
   const int avail = smem_optin - static_cast<int>(smem_extra()) - 16;
   return std::max(1, std::min(16, avail / (stage + 16)));
 }
@@ -1031,6 +1117,7 @@ struct Plan {
   int slots;
   size_t ws_bytes;
   int cluster;  // CTAs per cluster splitting K of one tile (1 = none)
+  int pair;     // CTA pairs (cta_group::2): tiles_x counts 256-row tiles
 };
 
 // Cluster size (1..8, at most the k-blocks) whose grid of tiles x size CTAs, one per
@@ -1098,7 +1185,16 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
                        t.tok_tile, t.w_tile);
     p->tn = t.w_tile;
   }
-  const int max_st = max_stages_for(p->tn, di.max_smem_optin);
+  // Split mode 4: CTA pairs (cta_group::2) on 128-token x 256-weight tiles, each pair a
+  // 256 x 256 tile; every CTA holds 128 token rows and 128 weight rows per stage.  The
+  // library's choice for prefill tiles with long K (>= 32 k-blocks), where each SM's TMA
+  // fill of 48 KB per k-block, not the tensor core, bounds the one-CTA tile.
+  if (t.split == 0 && !t.swap_ab && p->tn == 256 && K >= 4096) t.split = 4;
+  const bool pair = t.split == 4;
+  if (pair && (t.swap_ab || p->tn != 256))
+    return set_error(I8L_ENOTSUP, "CTA pairs (split 4) take tok_tile 128 x w_tile 256 tiles without swap_ab");
+  p->pair = pair ? 1 : 0;
+  const int max_st = max_stages_for(pair ? p->tn / 2 : p->tn, di.max_smem_optin);
   if (t.stages <= 0) {
     t.stages = max_st;
     // Decode tiles: leave room for a second CTA per SM (the next kernel under PDL).
@@ -1109,7 +1205,7 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   if (t.group <= 0) t.group = 1;
   const int rows_x = t.swap_ab ? N : M;
   const int rows_y = t.swap_ab ? M : N;
-  p->tiles_x = (rows_x + kXRows - 1) / kXRows;
+  p->tiles_x = (rows_x + (pair ? 2 * kXRows : kXRows) - 1) / (pair ? 2 * kXRows : kXRows);
   p->tiles_y = (rows_y + p->tn - 1) / p->tn;
   p->kblocks = (K + kBK - 1) / kBK;
   p->total_tiles = p->tiles_x * p->tiles_y;
@@ -1168,8 +1264,14 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
       p->dp_tiles = p->total_tiles;
     else
       p->dp_tiles = waves >= 1 ? (waves - 1) * ctas : 0;
+  } else if (split == 4) {
+    // One pair (two CTAs, one cluster) per 256 x 256 tile, persistent over the tiles.
+    const int pairs = std::max(1, std::min(p->total_tiles, (t.ctas > 0 ? t.ctas : di.sms) / 2));
+    ctas = 2 * pairs;
+    p->dp_tiles = p->total_tiles;
   } else if (split != 3) {
-    return set_error(I8L_ENOTSUP, "split mode %d unknown (0 auto, 1 whole, 2 stream-K, 3 cluster)", split);
+    return set_error(I8L_ENOTSUP,
+                     "split mode %d unknown (0 auto, 1 whole, 2 stream-K, 3 cluster, 4 CTA pairs)", split);
   }
   t.split = split;
   t.cluster = p->cluster;
@@ -1197,11 +1299,11 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   return I8L_OK;
 }
 
-template <int TN>
+template <int TN, bool kPair = false>
 static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const CUtensorMap &mo,
                      const CUtensorMap &mw, const GemmArgs &a, int ctas, int stages,
                      cudaStream_t stream) {
-  const size_t smem = SmemLayout<TN>::bytes(stages);
+  const size_t smem = SmemLayout<TN, kPair>::bytes(stages);
   // Largest dynamic shared memory already allowed, per device (the attribute is
   // set on the function as loaded in each device's context).
   static size_t configured[64] = {};
@@ -1209,12 +1311,13 @@ static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const CUtenso
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64 || smem > configured[dev]) {
-    e = cudaFuncSetAttribute(w8a8_gemm_sm100<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(w8a8_gemm_sm100<TN, kPair>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
-  e = launch(w8a8_gemm_sm100<TN>, dim3(ctas), dim3(kThreads), smem, stream, a.cluster, mx, my, mo,
+  e = launch(w8a8_gemm_sm100<TN, kPair>, dim3(ctas), dim3(kThreads), smem, stream,
+             kPair ? 2 : a.cluster, mx, my, mo,
              mw, a);
   if (e != cudaSuccess) return cuda_error(e, "gemm launch");
   e = cudaGetLastError();
@@ -1282,7 +1385,7 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   const int64_t xrows = swap ? N : M, yrows = swap ? M : N;
   const int64_t xld = swap ? ldw : lda, yld = swap ? lda : ldw;
   if ((e = make_operand_map(&mx, xp, xrows, K, xld, kXRows))) return e;
-  if ((e = make_operand_map(&my, yp, yrows, K, yld, p.tn))) return e;
+  if ((e = make_operand_map(&my, yp, yrows, K, yld, p.pair ? p.tn / 2 : p.tn))) return e;
 
   GemmArgs a{};
   a.M = M;
@@ -1340,6 +1443,7 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   a.status = status_ptr();
   a.cluster = p.cluster;
   a.act_direct = p.tile.act == 2 ? 1 : 0;
+  a.pair = p.pair;
   a.act = A;
   a.lda = lda;
   // Early cluster mode needs the (cluster-1) slots, each TN x 128 int32 apart, inside
@@ -1357,6 +1461,7 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
     case 128:
       return launch_tn<128>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     case 256:
+      if (p.pair) return launch_tn<256, true>(mx, my, mo, mw, a, p.ctas, a.stages, s);
       return launch_tn<256>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     default:
       return set_error(I8L_ENOTSUP, "no kernel for tile width %d", p.tn);

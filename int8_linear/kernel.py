@@ -55,7 +55,8 @@ class Config:
             choice gives the same bits: 0 the library's choice, 1 whole tiles, 2
             stream-K over the SMs (reduced in a workspace), 3 cluster split-K (the CTAs
             of a thread-block cluster split a tile's K and reduce over distributed
-            shared memory; swap_ab tiles of at most 64 tokens).
+            shared memory; swap_ab tiles of at most 64 tokens), 4 CTA pairs (two SMs
+            per 256 x 256 tile with 256-row tcgen05 MMAs; 128 x 256 tiles, no swap_ab).
     ctas    persistent CTAs, 0 for one per SM.
     cluster CTAs per cluster for split=3, 0 for the library's choice.
     store   output path: 0 the library's choice, 1 TMA stores, 2 plain stores.
@@ -83,7 +84,7 @@ class Config:
 
     @property
     def name(self) -> str:
-        tail = (" swap" if self.swapped else "") + {0: "", 1: " whole", 2: " sk", 3: " cl"}.get(
+        tail = (" swap" if self.swapped else "") + {0: "", 1: " whole", 2: " sk", 3: " cl", 4: " pair"}.get(
             self.split, f" split{self.split}")
         tail += str(self.cluster) if self.split == 3 and self.cluster else ""
         tail += f" c{self.ctas}" if self.ctas else ""
@@ -100,7 +101,7 @@ class Config:
                 raise NotSupported(f"{self.name}: swap_ab tiles are bm in {TOKEN_TILES} x bn 128")
         elif self.bm != 128 or self.bn not in (128, 256):
             raise NotSupported(f"{self.name}: tiles are bm 128 x bn in (128, 256)")
-        if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1, 2, 3):
+        if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1, 2, 3, 4):
             raise NotSupported(f"{self.name}: bad stages/group_m/split")
         if self.store not in (0, 1, 2) or self.act not in (0, 1, 2):
             raise NotSupported(f"{self.name}: store and act must be 0, 1 or 2")
@@ -108,6 +109,8 @@ class Config:
             raise NotSupported(f"{self.name}: direct activation loads take swap_ab tiles")
         if self.split == 3 and (not self.swapped or self.bm > 64 or not 0 <= self.cluster <= 8):
             raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles of <= 64 tokens")
+        if self.split == 4 and (self.swapped or self.bn != 256):
+            raise NotSupported(f"{self.name}: CTA pairs take 128 x 256 tiles without swap_ab")
 
     def as_tile(self) -> _native.I8LTile:
         return _native.I8LTile(
@@ -122,7 +125,7 @@ def default_config(m: int, n: int, k: int) -> Config:
     MMA side and the tokens on the narrow side, the smallest token tile that holds
     M; larger batches use 128 x 256 tiles.  The library then splits K when whole
     tiles would leave SMs idle: inside thread-block clusters for decode tiles, by
-    stream-K otherwise."""
+    stream-K otherwise.  Prefill with K >= 4096 uses CTA pairs (split 4)."""
     if m <= 256:
         return Config(next(t for t in TOKEN_TILES if t >= m), 128)
     # Prefill: the wider tile unless the narrower one fills the SMs clearly better.
@@ -131,7 +134,10 @@ def default_config(m: int, n: int, k: int) -> Config:
         tiles = -(-m // 128) * -(-n // bn)
         waves = -(-tiles // sms)
         return tiles / (waves * sms)
-    return Config(128, 256) if waves_eff(256) >= 0.8 * waves_eff(128) else Config(128, 128)
+    if waves_eff(256) < 0.8 * waves_eff(128):
+        return Config(128, 128)
+    # Long K: pairs of SMs per 256 x 256 tile (cta_group::2) halve each SM's weight fill.
+    return Config(128, 256, split=4) if k >= 4096 else Config(128, 256)
 
 
 @lru_cache(maxsize=None)

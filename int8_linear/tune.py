@@ -53,6 +53,8 @@ def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
     if m >= 64:
         for bn in (128, 256):
             out += [Config(128, bn, split=1), Config(128, bn, split=2)]
+    if m >= 256:   # CTA pairs: two SMs per 256 x 256 tile
+        out += [Config(128, 256, split=4), Config(128, 256, split=4, group_m=16)]
     seen, uniq = set(), []
     for c in out:
         if c.name in seen:

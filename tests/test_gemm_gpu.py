@@ -144,6 +144,27 @@ def test_declines_direct_activation_loads_it_cannot_take():
         w8a8_mm(a[:1], w.t(), one(), one(), config=Config(16, 128, split=1, act=2))
 
 
+@pytest.mark.parametrize("m,k,n", [(256, 256, 256), (300, 1040, 1000), (1024, 2048, 4096), (4096, 2048, 12288),
+                                   (513, 6144, 2056), (2000, 4096, 520)])
+def test_cta_pair_tiles_bit_exact(m, k, n):
+    """Two SMs per 256 x 256 tile (cta_group::2): each CTA loads its 128 token rows and
+    half of the weight tile, the even CTA issues the 256-row MMAs; the int32 product
+    and the bf16 output equal the one-CTA tiles'."""
+    a, w = ints((m, k), 70 + m), ints((n, k), 71)
+    g = torch.Generator().manual_seed(72)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    cfg = Config(128, 256, split=4)
+    want = exact(a, w)
+    assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), want)
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=cfg)
+    assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), "bf16"))
+    for ctas in (2, 6):   # fewer pairs than tiles: each pair walks several tiles
+        got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=Config(128, 256, split=4, ctas=ctas))
+        assert np.array_equal(np_(got), want), ctas
+
+
 def test_declines_a_cluster_whose_partial_sums_do_not_fit():
     a, w = ints((64, 2048), 1), ints((1024, 2048), 2)
     with pytest.raises(NotSupported, match="ring"):
