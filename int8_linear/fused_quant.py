@@ -28,6 +28,7 @@ import torch
 
 from int8_linear import _native
 from int8_linear._native import NotSupported
+from int8_linear.kernel import current_stream
 
 _ACT = {torch.bfloat16: _native.BF16, torch.float16: _native.F16}
 _WEIGHT = {torch.bfloat16: _native.BF16, torch.float16: _native.F16, torch.float32: _native.F32}
@@ -42,7 +43,7 @@ def _act_code(t: torch.Tensor) -> int:
 
 
 def _stream(t: torch.Tensor) -> int:
-    return torch.cuda.current_stream(t.device).cuda_stream
+    return current_stream(t.get_device())
 
 
 def add_rmsnorm_quant(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor,

@@ -168,14 +168,35 @@ def choose_config(m: int, n: int, k: int) -> Config:
 
 _DTYPE_CODE = {torch.bfloat16: _native.BF16, torch.float16: _native.F16, torch.float32: _native.F32}
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_tiles: dict[Config, _native.I8LTile] = {}
+# The current stream's raw handle without building a torch.cuda.Stream object (the host
+# cost of an eager call is a few microseconds, so each one counts).
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
-def workspace(device: torch.device, stream: int) -> torch.Tensor:
+def current_stream(device_index: int) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
+def _tile_of(cfg: Config) -> _native.I8LTile:
+    """The C tile struct of a validated config (checked and built once per config)."""
+    tile = _tiles.get(cfg)
+    if tile is None:
+        cfg.check()
+        tile = _tiles[cfg] = cfg.as_tile()
+    return tile
+
+
+def workspace(device: torch.device | int, stream: int) -> torch.Tensor:
     """The zero-filled split-K workspace for this device and stream (allocated once)."""
-    key = (device.index, stream)
+    index = device if isinstance(device, int) else device.index
+    key = (index, stream)
     ws = _workspaces.get(key)
     if ws is None:
-        ws = _workspaces[key] = torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8, device=device)
+        ws = _workspaces[key] = torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8,
+                                            device=torch.device("cuda", index))
     return ws
 
 
@@ -217,13 +238,13 @@ def w8a8_mm(
         raise ValueError(f"cannot multiply {tuple(a_q.shape)} by {tuple(b_q.shape)}")
     m, k = a_q.shape
     n = b_q.shape[1]
-    cfg = config or choose_config(m, n, k)
-    cfg.check()
+    tile = _tile_of(config or choose_config(m, n, k))
     if k % 16:
         raise NotSupported(f"K={k} must be a multiple of 16 (TMA rows of 16-byte granules)")
     if n > 1 and b_q.stride(0) != 1:
         raise NotSupported("B_q must be the K-contiguous [K, N] view of an [N, K] weight")
-    sa, sb = scale_a.reshape(-1).contiguous(), scale_b.reshape(-1).contiguous()
+    sa = scale_a if scale_a.is_contiguous() else scale_a.contiguous()
+    sb = scale_b if scale_b.is_contiguous() else scale_b.contiguous()
     if sa.dtype != torch.float32 or sb.dtype != torch.float32:
         raise NotSupported(f"float32 scales only, got {sa.dtype} and {sb.dtype}")
     if sa.numel() not in (1, m) or sb.numel() not in (1, n):
@@ -244,23 +265,27 @@ def w8a8_mm(
     if m == 0 or n == 0:
         return out
     a = _aligned_rows(a_q)
-    w = _aligned_rows(b_q.t())
+    # The weight's [N, K] rows are b_q's columns: row stride b_q.stride(1).
+    wp, ldw = b_q.data_ptr(), b_q.stride(1)
+    if b_q.stride(0) != 1 or wp % 16 or ldw % 16:
+        w = _aligned_rows(b_q.t())
+        wp, ldw = w.data_ptr(), w.stride(0)
     lib = _native.load()
-    stream = torch.cuda.current_stream(a_q.device).cuda_stream
-    ws = workspace(a_q.device, stream)
-    tile = cfg.as_tile()
-    if a_q.device.index != torch.cuda.current_device():
-        with torch.cuda.device(a_q.device):
-            code = _launch(lib, a, w, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream)
+    dev = a_q.get_device()
+    stream = current_stream(dev)
+    ws = workspace(dev, stream)
+    if dev != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            code = _launch(lib, a, wp, ldw, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream)
     else:
-        code = _launch(lib, a, w, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream)
+        code = _launch(lib, a, wp, ldw, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream)
     _native.check(code)
     return out
 
 
-def _launch(lib, a, w, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream) -> int:
+def _launch(lib, a, wp, ldw, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, ws, stream) -> int:
     return lib.i8l_w8a8_mm(
-        a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0),
+        a.data_ptr(), a.stride(0), wp, ldw,
         sa.data_ptr(), int(sa.numel() > 1), sb.data_ptr(), int(sb.numel() > 1),
         bias.data_ptr() if bias is not None else None,
         _DTYPE_CODE[bias.dtype] if bias is not None else 0,
