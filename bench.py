@@ -355,10 +355,13 @@ def run_ours(args, world, rank, dev):
         e2e = run_e2e(layers, acts, cases, dev, world, max(1, min(args.steps, 5)))
 
     del graphs
-    standin = quant = standin_tp = standin_tp_peer = None
+    standin = quant = standin_tp = standin_tp_peer = host = None
     if not args.no_standin and world == 1:
         standin = run_standin(dev)
         quant = run_quantisers(dev)
+        import int8_linear.vllm_patch  # noqa: F401  (registers the custom op)
+        from int8_linear import fused_quant as fq_ours
+        host = host_cost(w8a8_mm, torch.ops.int8_linear.w8a8_mm, fq_ours, dev)
     if not args.no_standin and world > 1:
         from int8_linear.tp import PeerComm
 
@@ -375,9 +378,44 @@ def run_ours(args, world, rank, dev):
         "l2_warm_us": warm, "roofline": roofline, "roofline_other": other,
         "allgather_us_per_sweep": allgather_us, "e2e": e2e, "standin_us_per_layer": standin,
         "quantisers": quant, "standin_tp_us_per_layer": standin_tp,
-        "standin_tp_peer_us_per_layer": standin_tp_peer,
+        "standin_tp_peer_us_per_layer": standin_tp_peer, "host_us_per_call": host,
         "clocks": clocks.summary(), "gpu_launches": launches,
     }
+
+
+def host_cost(mm, op, fq, dev) -> dict:
+    """The host side of an eager call: µs per call of back-to-back eager calls
+    at M=1 (qkv 2048 x 4096), where the host, not the GPU, sets the pace.  The same
+    function times both arms (`mm`/`op`/`fq` are the arm's w8a8_mm, custom op and
+    fused_quant module)."""
+    import time
+
+    import torch
+
+    a = torch.randint(-127, 128, (1, 2048), dtype=torch.int8, device=dev)
+    w = torch.randint(-127, 128, (4096, 2048), dtype=torch.int8, device=dev)
+    sa, sb = torch.rand((1, 1), device=dev), torch.rand((4096, 1), device=dev)
+    x = torch.randn((1, 2048), device=dev).to(torch.bfloat16)
+    gam = torch.ones(2048, device=dev, dtype=torch.bfloat16)
+    gu = torch.randn((1, 12288), device=dev).to(torch.bfloat16)
+    out = {}
+
+    def t(name, fn, n=2000):
+        for _ in range(200):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        t1 = time.perf_counter()
+        torch.cuda.synchronize()
+        out[name] = round((t1 - t0) / n * 1e6, 2)
+
+    t("w8a8_mm", lambda: mm(a, w.t(), sa, sb, torch.bfloat16))
+    t("custom_op_w8a8_mm", lambda: op(a, w.t(), sa, sb, torch.bfloat16, None))
+    t("add_rmsnorm_quant", lambda: fq.add_rmsnorm_quant(x, x, gam, 1e-6, True))
+    t("silu_mul_quant", lambda: fq.silu_mul_quant(gu, True, True))
+    return out
 
 
 def run_e2e(layers, acts, cases, dev, world, passes):
@@ -661,8 +699,10 @@ def run_reference_triton_child(args):
         standin[str(m)] = round(statistics.median([time_graph(capture(step)) for _ in range(3)]) / 28, 2)
         del layers
         torch.cuda.empty_cache()
+    import int8_linear.vllm_patch  # noqa: F401  (registers the reference's custom op)
+    host = host_cost(ref_mm, torch.ops.int8_linear.w8a8_mm, rfq, dev)
     print(json.dumps({"value": round(total, 2), "per_shape_us": per, "standin_us_per_layer": standin,
-                      "quantisers": quant,
+                      "quantisers": quant, "host_us_per_call": host,
                       "standin_o_proj_quantiser": qsrc, "triton": __import__("triton").__version__}))
 
 
