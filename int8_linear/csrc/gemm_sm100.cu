@@ -41,7 +41,6 @@ constexpr int kBK = 128;        // K bytes per stage: one 128-byte swizzle row
 constexpr int kXRows = 128;     // MMA M
 constexpr int kThreads = 192;   // 6 warps
 constexpr int kEpiWarps = 4;
-constexpr int kXBytes = kXRows * kBK;  // 16 KB
 
 struct GemmArgs {
   int M, N, K;
@@ -290,6 +289,45 @@ __device__ __forceinline__ void epilogue_direct(const GemmArgs &a, const TileCtx
   }
 }
 
+// Narrow tiles: 8 consecutive outputs of token row m (tile columns c0..c0+7), dequantised
+// (sa: the row's scale) and stored with one 16-byte store (32 bytes for 32-bit outputs)
+// where the row allows.
+template <int TN>
+__device__ __forceinline__ void store_row8(const GemmArgs &a, const TileCtx &t, int m, int c0,
+                                           float sa, const uint32_t (&r)[8]) {
+  const bool raw = a.out_dtype == I8L_I32;
+  const bool has_bias = a.bias != nullptr;
+  const bool narrow16 = a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16;
+  const int n0 = t.ty * TN + c0;
+  const int nv = min(8, a.N - n0);
+  uint32_t bits[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int acc = static_cast<int>(r[j]);
+    const float v = raw ? 0.f : dequant(acc, sa, t.s_col[c0 + j], t.b_col[c0 + j], has_bias);
+    bits[j] = narrow16 ? out_bits16(a.out_dtype, v) : out_bits32(a.out_dtype, acc, v);
+  }
+  const long long idx = static_cast<long long>(m) * a.ldc + n0;
+  if (a.vec_store && nv == 8) {
+    if (narrow16) {
+      *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.out) + idx) =
+          make_uint4(bits[0] | (bits[1] << 16), bits[2] | (bits[3] << 16), bits[4] | (bits[5] << 16),
+                     bits[6] | (bits[7] << 16));
+    } else {
+      uint4 *p = reinterpret_cast<uint4 *>(static_cast<uint32_t *>(a.out) + idx);
+      p[0] = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+      p[1] = make_uint4(bits[4], bits[5], bits[6], bits[7]);
+    }
+    return;
+  }
+  for (int j = 0; j < nv; ++j) {
+    if (narrow16)
+      static_cast<uint16_t *>(a.out)[idx + j] = static_cast<uint16_t>(bits[j]);
+    else
+      static_cast<uint32_t *>(a.out)[idx + j] = bits[j];
+  }
+}
+
 // Number of accumulator columns of a tile that hold real (in-range) Y rows.
 template <int TN>
 __device__ __forceinline__ int live_cols(const GemmArgs &a, int ty) {
@@ -322,9 +360,16 @@ constexpr int kStagingBytes = kEpiWarps * 2 * kStageBufBytes;   // 16 KB
 constexpr int kScalFloats = 256;                                // per array per buffer
 constexpr int kScalBytes = 2 * 2 * kScalFloats * 4;             // [2 arrays][2 acc][256]
 
-template <int TN, bool kPair = false>
+// Kernel variants: 0 one CTA per tile; 1 CTA pairs (cta_group::2, 256-row tiles);
+// 2 narrow (decode batches of <= 16 tokens with the weight on the N side: 64-row
+// token tile, 256 weight rows per MMA, one accumulator so two CTAs share an SM).
+constexpr int kVarOne = 0, kVarPair = 1, kVarNarrow = 2;
+
+template <int TN, int kVar = kVarOne>
 struct SmemLayout {
-  static constexpr int kYRows = kPair ? TN / 2 : TN;  // Y rows this CTA holds per stage
+  static constexpr int kXRowsV = kVar == kVarNarrow ? 64 : kXRows;  // X rows per stage
+  static constexpr int kXBytes = kXRowsV * kBK;
+  static constexpr int kYRows = kVar == kVarPair ? TN / 2 : TN;     // Y rows this CTA holds
   static constexpr int kYBytes = kYRows * kBK;
   static constexpr int kStageBytes = kXBytes + kYBytes;
   // Decode tiles rotate their k-steps over several accumulators: a chain of
@@ -333,7 +378,9 @@ struct SmemLayout {
   // addition is exact and order-free).  Two accumulators (double buffer) x chains.
   static constexpr int kChains = TN <= 16 ? 4 : (TN <= 64 ? 2 : 1);
   static constexpr int kAccCols = kChains * TN;
-  static constexpr int kTmemCols = (2 * kAccCols < 32) ? 32 : 2 * kAccCols;
+  // Narrow tiles keep one accumulator (one tile per CTA), so two CTAs fit an SM's TMEM.
+  static constexpr int kAccBufs = kVar == kVarNarrow ? 1 : 2;
+  static constexpr int kTmemCols = (kAccBufs * kAccCols < 32) ? 32 : kAccBufs * kAccCols;
   // stages | staging | scales | barriers: full[S], empty[S], acc_full[2],
   // acc_empty[2], drain, peer, done, act | tmem slot, flags
   static size_t bytes(int stages) {
@@ -500,13 +547,15 @@ __device__ __forceinline__ void load_act_direct(const GemmArgs &a, uint8_t *sy, 
 
 // Decode tiles (TN <= 64) cap registers so two CTAs fit on an SM: with programmatic
 // dependent launch the next GEMM's CTA streams its weights beside this one.
-template <int TN, bool kPair>
-__global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
+template <int TN, int kVar>
+__global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2 : 1)
     w8a8_gemm_sm100(const __grid_constant__ CUtensorMap map_x,
                     const __grid_constant__ CUtensorMap map_y,
                     const __grid_constant__ CUtensorMap map_out,
                     const __grid_constant__ CUtensorMap map_ws, const GemmArgs a) {
-  using L = SmemLayout<TN, kPair>;
+  constexpr bool kPair = kVar == kVarPair;
+  constexpr bool kNarrow = kVar == kVarNarrow;
+  using L = SmemLayout<TN, kVar>;
   // CTA pairs: rank 1 loads its halves and runs its epilogue; rank 0 also issues the MMAs.
   const int rank = kPair ? static_cast<int>(blockIdx.x & 1u) : 0;
   const bool leader = rank == 0;
@@ -515,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int S = a.stages;
   uint8_t *sx = smem;
-  uint8_t *sy = smem + static_cast<size_t>(S) * kXBytes;
+  uint8_t *sy = smem + static_cast<size_t>(S) * L::kXBytes;
   uint8_t *staging = smem + static_cast<size_t>(S) * L::kStageBytes;
   float *scal = reinterpret_cast<float *>(staging + kStagingBytes);
   uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(scal) + kScalBytes);
@@ -548,11 +597,13 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     mbar_init(act_bar, kEpiWarps);
     if (a.cluster_early && cluster_ctarank() == 0) {
       // One tile per cluster: its partial sums arrive as (cluster-1) slots of the
-      // live column chunks.  Armed before the cluster sync, so before any byte lands.
+      // live column chunks (narrow tiles: of the M token rows only).  Armed before the
+      // cluster sync, so before any byte lands.
       int tx, ty;
       tile_coords(a, static_cast<int>(blockIdx.x) / a.cluster, tx, ty);
       const int nch = (live_cols<TN>(a, ty) + 15) / 16;
-      mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * kXRows * 4));
+      const int rows = kNarrow ? a.M : kXRows;
+      mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * rows * 4));
     }
     *abort_flag = 0;
     *last_flag = 0;
@@ -595,10 +646,10 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
       // TN Y rows, counted on the even CTA's `full` barrier.
       auto load_x = [&](int st, int kb, int tx) {
         if constexpr (kPair)
-          tma_load_2d_pair(sx + static_cast<size_t>(st) * kXBytes, &map_x,
+          tma_load_2d_pair(sx + static_cast<size_t>(st) * L::kXBytes, &map_x,
                            map_to_rank(smem_u32(&full[st]), 0), kb * kBK, tx * kXRows, pol_x);
         else
-          tma_load_2d(sx + static_cast<size_t>(st) * kXBytes, &map_x, &full[st], kb * kBK,
+          tma_load_2d(sx + static_cast<size_t>(st) * L::kXBytes, &map_x, &full[st], kb * kBK,
                       tx * kXRows, pol_x);
       };
       auto load_y = [&](int st, int kb, int ty) {
@@ -613,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
       // Bytes one stage's `full` barrier waits for (both CTAs' with pairs; armed by the
       // even CTA only).
       const uint32_t stage_tx = kPair ? 2u * L::kStageBytes
-                                      : (a.act_direct ? static_cast<uint32_t>(kXBytes) : L::kStageBytes);
+                                      : (a.act_direct ? static_cast<uint32_t>(L::kXBytes) : L::kStageBytes);
       // Weight tiles of the first stages are loaded before waiting for the previous
       // kernel: inference weights are never written by the kernel just before.  The
       // weight is X with swap_ab, else Y.  Activations wait for pdl_wait().
@@ -692,7 +743,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
     // ------------------------------------------------------------ MMA issuer
     // (CTA pairs: the even CTA issues the 256-row MMAs for both.)
     if (lane == 0 && leader) {
-      constexpr uint32_t kIdesc = idesc_i8(kPair ? 2 * kXRows : kXRows, TN);
+      constexpr uint32_t kIdesc = idesc_i8(kPair ? 2 * kXRows : L::kXRowsV, TN);
       Schedule sch;
       sch.init(a);
       Segment seg;
@@ -723,7 +774,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sw128_kmajor_desc(smem_u32(sx + static_cast<size_t>(stage) * kXBytes));
+          const uint64_t ad = sw128_kmajor_desc(smem_u32(sx + static_cast<size_t>(stage) * L::kXBytes));
           const uint64_t bd = sw128_kmajor_desc(smem_u32(sy + static_cast<size_t>(stage) * L::kYBytes));
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k, ++kstep) {
@@ -750,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           mma_commit_pair_mc(&acc_full[acc], 0x3);  // both CTAs' epilogues may read
         else
           mma_commit(&acc_full[acc]);
-        if (++acc == 2) {
+        if (++acc == L::kAccBufs) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -827,6 +878,10 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
         } else {
           const int m = t.tx * kXRows + row;
           if (m < a.M) t.s_row = a.sa_per_row ? a.sa[m] : a.sa[0];
+          if constexpr (kNarrow) {
+            // Token-row scales in the second accumulator's (unused) scale slot.
+            if (epi_tid < a.M) scal[kScalFloats + epi_tid] = a.sa_per_row ? a.sa[epi_tid] : a.sa[0];
+          }
           for (int c = epi_tid; c < TN; c += kEpiWarps * 32) {
             const int n = t.ty * TN + c;
             s_col[c] = n < a.N ? (a.sb_per_col ? a.sb[n] : a.sb[0]) : 0.f;
@@ -841,7 +896,97 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
       if (!named_bar_and(2, kEpiWarps * 32, ok)) break;
       tc_fence_after();
       const bool whole = seg.kb0 == 0 && seg.kb1 == a.kblocks;
-      if (a.cluster > 1) {
+      if constexpr (kNarrow) {
+        // Narrow tiles: the M <= 16 token rows are TMEM lanes 0..M-1, which only warp
+        // quarter 0 can read.  That warp copies its rows' 256 int32 sums into `rows`
+        // (shared memory); then all four epilogue warps work on 8-column groups: a
+        // contributor pushes the groups into its slot of the leader (partial sums of
+        // [M rows][TN] int32 per contributor: in the leader's staging area when early,
+        // else in its idle operand ring after the go signal); the leader adds the slots
+        // to its own rows, dequantises and stores.
+        const int nch = (t.ncols + 15) / 16;
+        const int ngroups = a.M * (TN / 8);
+        const uint32_t rank = a.cluster > 1 ? cluster_ctarank() : 0u;
+        uint32_t *slots = reinterpret_cast<uint32_t *>(a.cluster_early ? staging : sx);
+        uint32_t *rows = reinterpret_cast<uint32_t *>(a.cluster_early ? sx : staging);
+        // `rows` holds token row m's 16-byte units at u ^ (m & 7): the quarter-0 lanes
+        // store whole rows at a 1 KB stride, which would otherwise all hit one bank.
+        if (quarter == 0) {
+          for (int c = 0; c < nch; c += 4) {
+            uint32_t r[4][16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (c + j < nch) tmem_ld16(t.taddr + (c + j) * 16, r[j]);
+            tmem_ld_wait();
+            if (lane < a.M) {
+              uint4 *dst = reinterpret_cast<uint4 *>(rows + lane * TN);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                if (c + j < nch)
+#pragma unroll
+                  for (int v = 0; v < 4; ++v)
+                    dst[((c + j) * 4 + v) ^ (lane & 7)] =
+                        make_uint4(r[j][4 * v], r[j][4 * v + 1], r[j][4 * v + 2], r[j][4 * v + 3]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release_acc(&acc_empty[acc]);
+        named_bar_sync(1, kEpiWarps * 32);  // `rows` complete
+        if (a.cluster > 1 && rank != 0) {
+          const bool go = a.cluster_early ||
+                          __all_sync(0xffffffffu, mbar_wait_cluster_bounded(
+                                                      done_bar, 0, abort_flag, a.status,
+                                                      kStatusClusterWait));
+          if (go) {
+            const uint32_t bar0 = map_to_rank(smem_u32(peer_bar), 0);
+            for (int gidx = epi_tid; gidx < ngroups; gidx += kEpiWarps * 32) {
+              const int m = gidx / (TN / 8), c = (gidx % (TN / 8)) * 8;
+              if (c >= nch * 16) continue;
+              const uint4 *src = reinterpret_cast<const uint4 *>(rows + m * TN);
+              const int u = c / 4;
+              const uint32_t dst = map_to_rank(
+                  smem_u32(slots + ((static_cast<size_t>(rank) - 1) * a.M + m) * TN + c), 0);
+              st_async_v4(dst, src[u ^ (m & 7)], bar0);
+              st_async_v4(dst + 16, src[(u + 1) ^ (m & 7)], bar0);
+            }
+          }
+        } else {
+          bool got = true;
+          if (a.cluster > 1) {
+            if (epi_tid == 0 && !a.cluster_early) {
+              mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * a.M * 4));
+              for (int p = 1; p < a.cluster; ++p)
+                mbar_arrive_remote(map_to_rank(smem_u32(done_bar), static_cast<uint32_t>(p)));
+            }
+            got = __all_sync(0xffffffffu, mbar_wait_bounded(peer_bar, 0, abort_flag, a.status,
+                                                             kStatusClusterWait));
+          }
+          if (got) {
+            const float *sa_rows = scal + kScalFloats;  // the second accumulator's scale slot
+            for (int gidx = epi_tid; gidx < ngroups; gidx += kEpiWarps * 32) {
+              const int m = gidx / (TN / 8), c = (gidx % (TN / 8)) * 8;
+              if (c >= t.ncols) continue;
+              uint32_t r[8];
+              {
+                const uint4 *src = reinterpret_cast<const uint4 *>(rows + m * TN);
+                const uint4 q0 = src[(c / 4) ^ (m & 7)], q1 = src[(c / 4 + 1) ^ (m & 7)];
+                r[0] = q0.x; r[1] = q0.y; r[2] = q0.z; r[3] = q0.w;
+                r[4] = q1.x; r[5] = q1.y; r[6] = q1.z; r[7] = q1.w;
+              }
+              for (int p = 1; p < a.cluster; ++p) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(
+                    slots + ((static_cast<size_t>(p) - 1) * a.M + m) * TN + c);
+                const uint4 q0 = src[0], q1 = src[1];
+                r[0] += q0.x; r[1] += q0.y; r[2] += q0.z; r[3] += q0.w;
+                r[4] += q1.x; r[5] += q1.y; r[6] += q1.z; r[7] += q1.w;
+              }
+              store_row8<TN>(a, t, m, c, sa_rows[m], r);
+            }
+          }
+        }
+      } else if (a.cluster > 1) {
         // Cluster split-K.  Once a CTA's MMAs are done its operand ring is idle.  The
         // leader (rank 0) then arms its receive barrier and tells each contributor to
         // go; contributors push their int32 partial sums into slot rank-1 of the
@@ -1010,7 +1155,7 @@ __global__ void __launch_bounds__(kThreads, TN <= 64 ? 2 : 1)
           if (epi_tid == 0) atomicExch(a.counters + slot, 0);
         }
       }
-      if (++acc == 2) {
+      if (++acc == L::kAccBufs) {
         acc = 0;
         acc_phase ^= 1u;
       }
@@ -1099,9 +1244,10 @@ static size_t smem_extra() { return 1024 + kStagingBytes + kScalBytes + 8 * 8 + 
 // Shared memory of one of two CTAs that share an SM (228 KB minus 1 KB reserved per CTA).
 constexpr int kHalfSmem = 233472 / 2 - 1024;
 
-// `y_rows`: Y rows one CTA holds per stage (TN, or TN/2 for a CTA pair).
-static int max_stages_for(int y_rows, int smem_optin) {
-  const int stage = kXBytes + y_rows * kBK;
+// X and Y rows one CTA holds per stage (X: 128, or 64 for narrow tiles; Y: TN, or
+// TN/2 for a CTA pair).
+static int max_stages_for(int y_rows, int smem_optin, int x_rows = kXRows) {
+  const int stage = x_rows * kBK + y_rows * kBK;
   const int avail = smem_optin - static_cast<int>(smem_extra()) - 16;
   return std::max(1, std::min(16, avail / (stage + 16)));
 }
@@ -1118,6 +1264,7 @@ struct Plan {
   size_t ws_bytes;
   int cluster;  // CTAs per cluster splitting K of one tile (1 = none)
   int pair;     // CTA pairs (cta_group::2): tiles_x counts 256-row tiles
+  int narrow;   // narrow decode tiles: <= 16 tokens x 256 weight rows, 64-row MMAs
 };
 
 // Cluster size (1..8, at most the k-blocks) whose grid of tiles x size CTAs, one per
@@ -1194,18 +1341,26 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   if (pair && (t.swap_ab || p->tn != 256))
     return set_error(I8L_ENOTSUP, "CTA pairs (split 4) take tok_tile 128 x w_tile 256 tiles without swap_ab");
   p->pair = pair ? 1 : 0;
-  const int max_st = max_stages_for(pair ? p->tn / 2 : p->tn, di.max_smem_optin);
+  // Narrow decode tiles: cluster split-K (split 3) on 128 x 256 tiles without swap_ab,
+  // for batches of <= 16 tokens: 64-row token tiles, the weight on the MMA's N side.
+  const bool narrow = t.split == 3 && !t.swap_ab;
+  if (narrow && (p->tn != 256 || M > 16))
+    return set_error(I8L_ENOTSUP, "narrow tiles (split 3 without swap_ab) take w_tile 256 and M <= 16");
+  p->narrow = narrow ? 1 : 0;
+  const int x_rows = narrow ? 64 : kXRows;
+  const int max_st = max_stages_for(pair ? p->tn / 2 : p->tn, di.max_smem_optin, x_rows);
   if (t.stages <= 0) {
     t.stages = max_st;
     // Decode tiles: leave room for a second CTA per SM (the next kernel under PDL).
-    if (t.swap_ab && p->tn <= 64) t.stages = std::max(2, std::min(max_st, max_stages_for(p->tn, kHalfSmem)));
+    if ((t.swap_ab && p->tn <= 64) || narrow)
+      t.stages = std::max(2, std::min(max_st, max_stages_for(p->tn, kHalfSmem, x_rows)));
   }
   if (t.stages < 2 || t.stages > max_st)
     return set_error(I8L_ENOTSUP, "stages %d outside [2, %d] for this tile", t.stages, max_st);
   if (t.group <= 0) t.group = 1;
   const int rows_x = t.swap_ab ? N : M;
   const int rows_y = t.swap_ab ? M : N;
-  p->tiles_x = (rows_x + (pair ? 2 * kXRows : kXRows) - 1) / (pair ? 2 * kXRows : kXRows);
+  p->tiles_x = narrow ? 1 : (rows_x + (pair ? 2 * kXRows : kXRows) - 1) / (pair ? 2 * kXRows : kXRows);
   p->tiles_y = (rows_y + p->tn - 1) / p->tn;
   p->kblocks = (K + kBK - 1) / kBK;
   p->total_tiles = p->tiles_x * p->tiles_y;
@@ -1234,11 +1389,14 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
     }
   }
   if (split == 3) {
-    if (!t.swap_ab || p->tn > 64)
+    if (!narrow && (!t.swap_ab || p->tn > 64))
       return set_error(I8L_ENOTSUP, "cluster split-K takes swap_ab tiles of at most 64 tokens");
-    // The leader's operand ring receives (cluster-1) partial-sum slots of TN x 128 int32.
-    const long long ring = static_cast<long long>(t.stages) * (kXBytes + p->tn * kBK);
-    auto fits = [&](int c) { return static_cast<long long>(c - 1) * p->tn * kXRows * 4 <= ring; };
+    // The leader's operand ring receives (cluster-1) partial-sum slots: TN x 128 int32
+    // (swap_ab tiles), or M token rows x TN int32 (narrow tiles).
+    const long long ring = static_cast<long long>(t.stages) * (x_rows * kBK + p->tn * kBK);
+    const long long slot = narrow ? static_cast<long long>(M) * p->tn * 4
+                                  : static_cast<long long>(p->tn) * kXRows * 4;
+    auto fits = [&](int c) { return static_cast<long long>(c - 1) * slot <= ring; };
     int cs = t.cluster;
     if (cs <= 0) {
       cs = best_cluster(p->total_tiles, p->kblocks, ctas);
@@ -1249,7 +1407,7 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
                        "cluster size %d outside [1, min(8, k-blocks=%d)] or its partial sums "
                        "exceed the %lld-byte ring",
                        cs, p->kblocks, ring);
-    if (cs == 1) split = 1;
+    if (cs == 1 && !narrow) split = 1;
     p->cluster = cs;
     ctas = p->total_tiles * cs;
     p->dp_tiles = p->total_tiles;
@@ -1299,11 +1457,11 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   return I8L_OK;
 }
 
-template <int TN, bool kPair = false>
+template <int TN, int kVar = kVarOne>
 static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const CUtensorMap &mo,
                      const CUtensorMap &mw, const GemmArgs &a, int ctas, int stages,
                      cudaStream_t stream) {
-  const size_t smem = SmemLayout<TN, kPair>::bytes(stages);
+  const size_t smem = SmemLayout<TN, kVar>::bytes(stages);
   // Largest dynamic shared memory already allowed, per device (the attribute is
   // set on the function as loaded in each device's context).
   static size_t configured[64] = {};
@@ -1311,13 +1469,13 @@ static int launch_tn(const CUtensorMap &mx, const CUtensorMap &my, const CUtenso
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64 || smem > configured[dev]) {
-    e = cudaFuncSetAttribute(w8a8_gemm_sm100<TN, kPair>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(w8a8_gemm_sm100<TN, kVar>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
-  e = launch(w8a8_gemm_sm100<TN, kPair>, dim3(ctas), dim3(kThreads), smem, stream,
-             kPair ? 2 : a.cluster, mx, my, mo,
+  e = launch(w8a8_gemm_sm100<TN, kVar>, dim3(ctas), dim3(kThreads), smem, stream,
+             kVar == kVarPair ? 2 : a.cluster, mx, my, mo,
              mw, a);
   if (e != cudaSuccess) return cuda_error(e, "gemm launch");
   e = cudaGetLastError();
@@ -1384,7 +1542,7 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   const int8_t *yp = swap ? A : W;
   const int64_t xrows = swap ? N : M, yrows = swap ? M : N;
   const int64_t xld = swap ? ldw : lda, yld = swap ? lda : ldw;
-  if ((e = make_operand_map(&mx, xp, xrows, K, xld, kXRows))) return e;
+  if ((e = make_operand_map(&mx, xp, xrows, K, xld, p.narrow ? 64 : kXRows))) return e;
   if ((e = make_operand_map(&my, yp, yrows, K, yld, p.pair ? p.tn / 2 : p.tn))) return e;
 
   GemmArgs a{};
@@ -1414,7 +1572,8 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   a.vec_store = aligned_out ? 1 : 0;
   // Output path: TMA stores through shared memory, or plain stores (cheaper for the
   // few rows of a decode batch).  store: 0 auto, 1 TMA, 2 direct.
-  const int store = tile && tile->store ? tile->store : ((swap && M <= 32) ? 2 : 1);
+  // Narrow tiles always store directly (one warp writes the few token rows).
+  const int store = p.narrow ? 2 : (tile && tile->store ? tile->store : ((swap && M <= 32) ? 2 : 1));
   CUtensorMap mo{}, mw{};
   if (aligned_out && store == 1) {
     static const CUtensorMapDataType kTypes[4] = {
@@ -1448,8 +1607,11 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   a.lda = lda;
   // Early cluster mode needs the (cluster-1) slots, each TN x 128 int32 apart, inside
   // the leader's staging area, which plain stores leave unused.
-  if (p.cluster > 1 && !a.tma_out)
-    a.cluster_early = static_cast<long long>(p.cluster - 1) * p.tn * kXRows * 4 <= kStagingBytes ? 1 : 0;
+  if (p.cluster > 1 && !a.tma_out) {
+    const long long slot = p.narrow ? static_cast<long long>(M) * p.tn * 4
+                                    : static_cast<long long>(p.tn) * kXRows * 4;
+    a.cluster_early = static_cast<long long>(p.cluster - 1) * slot <= kStagingBytes ? 1 : 0;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (p.tn) {
     case 16:
@@ -1461,7 +1623,8 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
     case 128:
       return launch_tn<128>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     case 256:
-      if (p.pair) return launch_tn<256, true>(mx, my, mo, mw, a, p.ctas, a.stages, s);
+      if (p.pair) return launch_tn<256, kVarPair>(mx, my, mo, mw, a, p.ctas, a.stages, s);
+      if (p.narrow) return launch_tn<256, kVarNarrow>(mx, my, mo, mw, a, p.ctas, a.stages, s);
       return launch_tn<256>(mx, my, mo, mw, a, p.ctas, a.stages, s);
     default:
       return set_error(I8L_ENOTSUP, "no kernel for tile width %d", p.tn);

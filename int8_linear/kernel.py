@@ -55,7 +55,9 @@ class Config:
             choice gives the same bits: 0 the library's choice, 1 whole tiles, 2
             stream-K over the SMs (reduced in a workspace), 3 cluster split-K (the CTAs
             of a thread-block cluster split a tile's K and reduce over distributed
-            shared memory; swap_ab tiles of at most 64 tokens), 4 CTA pairs (two SMs
+            shared memory; swap_ab tiles of at most 64 tokens, or, without swap_ab, narrow
+            128 x 256 tiles for batches of <= 16 tokens: the weight on the MMA's N side,
+            256 weight rows per MMA instruction), 4 CTA pairs (two SMs
             per 256 x 256 tile with 256-row tcgen05 MMAs; 128 x 256 tiles, no swap_ab).
     ctas    persistent CTAs, 0 for one per SM.
     cluster CTAs per cluster for split=3, 0 for the library's choice.
@@ -107,8 +109,11 @@ class Config:
             raise NotSupported(f"{self.name}: store and act must be 0, 1 or 2")
         if self.act == 2 and not self.swapped:
             raise NotSupported(f"{self.name}: direct activation loads take swap_ab tiles")
-        if self.split == 3 and (not self.swapped or self.bm > 64 or not 0 <= self.cluster <= 8):
-            raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles of <= 64 tokens")
+        if self.split == 3 and not 0 <= self.cluster <= 8:
+            raise NotSupported(f"{self.name}: clusters hold at most 8 CTAs")
+        if self.split == 3 and (self.bm > 64 if self.swapped else self.bn != 256):
+            raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles of <= 64 tokens "
+                               "or narrow 128 x 256 tiles (batches of <= 16 tokens)")
         if self.split == 4 and (self.swapped or self.bn != 256):
             raise NotSupported(f"{self.name}: CTA pairs take 128 x 256 tiles without swap_ab")
 
@@ -125,7 +130,13 @@ def default_config(m: int, n: int, k: int) -> Config:
     MMA side and the tokens on the narrow side, the smallest token tile that holds
     M; larger batches use 128 x 256 tiles.  The library then splits K when whole
     tiles would leave SMs idle: inside thread-block clusters for decode tiles, by
-    stream-K otherwise.  Prefill with K >= 4096 uses CTA pairs (split 4)."""
+    stream-K otherwise.  Prefill with K >= 4096 uses CTA pairs (split 4).  Batches of
+    one or two tokens on moderate weights (K 1024..6144, N <= 8192) take narrow tiles
+    instead: 256 weight rows per MMA, K split over a cluster of up to 8 CTAs with at
+    least two 128-wide k-blocks each (measured faster there on B200; larger weights
+    have too few 256-row tiles to fill the SMs)."""
+    if m <= 2 and 1024 <= k <= 6144 and n <= 8192:
+        return Config(128, 256, split=3, cluster=min(8, k // 256))
     if m <= 256:
         return Config(next(t for t in TOKEN_TILES if t >= m), 128)
     # Prefill: the wider tile unless the narrower one fills the SMs clearly better.

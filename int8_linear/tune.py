@@ -47,6 +47,8 @@ def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
                 # activation by plain loads after the dependency wait (where it fits)
                 out += [Config(tn, 128, split=3, cluster=c, act=a) for c in (2, 3, 4, 8) for a in (1, 2)]
                 out += [Config(tn, 128, split=1, ctas=tiles, act=2)]
+            if m <= 16:   # narrow tiles: the weight on the MMA's N side (256 rows per MMA)
+                out += [Config(128, 256, split=3, cluster=c) for c in (1, 2, 3, 4, 6, 8)]
             if m <= 32:   # plain versus TMA stores for the few output rows
                 out += [Config(tn, 128, split=3, cluster=c, store=1) for c in (2, 4)]
                 out += [Config(tn, 128, split=1, store=1), Config(tn, 128, split=2, store=2)]

@@ -1,0 +1,42 @@
+"""Tile choices on the host: the untuned heuristic and the committed B200 table give
+tilings that a B200 kernel exists for (no GPU needed)."""
+
+from __future__ import annotations
+
+import json
+
+import pytest
+
+from int8_linear.kernel import TUNED_PATH, Config, default_config
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 16, 17, 64, 256, 257, 4096])
+@pytest.mark.parametrize("k,n", [(2048, 4096), (1024, 2048), (6144, 2048), (14336, 4096), (512, 2048),
+                                 (4096, 28672), (2048, 12288)])
+def test_default_config_is_a_valid_tiling(m, k, n):
+    default_config(m, n, k).check()
+
+
+def test_one_and_two_token_batches_default_to_narrow_tiles_on_moderate_weights():
+    cfg = default_config(1, 4096, 2048)
+    assert (cfg.bm, cfg.bn, cfg.split, cfg.cluster, cfg.swapped) == (128, 256, 3, 8, False)
+    assert default_config(2, 2048, 1024).cluster == 4            # two k-blocks per CTA
+    assert default_config(1, 12288, 2048).swapped                # too few 256-row tiles
+    assert default_config(1, 4096, 14336).swapped                # long K: swap tiles
+    assert default_config(3, 4096, 2048).swapped                 # beyond two tokens: swap tiles
+
+
+def test_tuned_table_entries_are_valid_tilings():
+    tables = json.loads(TUNED_PATH.read_text())
+    count = 0
+    for shapes in tables.values():
+        for shape, buckets in shapes.items():
+            k, n = (int(x) for x in shape.split("x"))
+            for m, entry in buckets.items():
+                cfg = Config(**entry["config"])
+                cfg.check()
+                if cfg.split == 3 and not cfg.swapped:   # narrow tiles take <= 16 tokens
+                    assert int(m) <= 16, (shape, m)
+                assert entry["graph_us"] > 0
+                count += 1
+    assert count > 0

@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from int8_linear import Config, NotSupported, _native, w8a8_mm
-from int8_linear.kernel import choose_config, default_config
+from int8_linear.kernel import TOKEN_TILES, choose_config
 from oracle import gemm as og
 from oracle.numerics import to_bits
 from tests.gpu_util import bits, ints, np_, offset_ints
@@ -25,6 +25,11 @@ SHAPES = [(1, 2048, 2048), (3, 2048, 1024), (17, 2048, 6144), (64, 2048, 2048), 
 
 def exact(a: torch.Tensor, w: torch.Tensor) -> np.ndarray:
     return og.exact(np_(a), np_(w))
+
+
+def tok_tile(m):
+    """The smallest swap_ab token tile that holds M rows."""
+    return next(t for t in TOKEN_TILES if t >= m)
 
 
 def one():
@@ -126,7 +131,7 @@ def test_direct_activation_loads_bit_exact(m, k, n, split, cluster):
     sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
     sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
-    bm = default_config(m, n, k).bm
+    bm = tok_tile(m)
     want_raw = exact(a, w)
     want = to_bits(og.epilogue_f32(want_raw, np_(sa), np_(sb), np_(bias)), "bf16")
     for act in (1, 2):
@@ -163,6 +168,36 @@ def test_cta_pair_tiles_bit_exact(m, k, n):
     for ctas in (2, 6):   # fewer pairs than tiles: each pair walks several tiles
         got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=Config(128, 256, split=4, ctas=ctas))
         assert np.array_equal(np_(got), want), ctas
+
+
+@pytest.mark.parametrize("m", [1, 2, 5, 16])
+@pytest.mark.parametrize("k,n,cluster", [(2048, 4096, 8), (2048, 2048, 4), (6144, 2048, 8), (2048, 12288, 3),
+                                         (1040, 1000, 4), (256, 520, 1), (2048, 4096, 2)])
+def test_narrow_tiles_bit_exact(m, k, n, cluster):
+    """Decode batches with the weight on the MMA's N side (64-row token tile x 256 weight
+    rows, cluster split-K over DSMEM): same bits as the swap_ab tiles and the oracle."""
+    a, w = ints((m, k), 60 + m), ints((n, k), 61)
+    g = torch.Generator().manual_seed(62)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    cfg = Config(128, 256, split=3, cluster=cluster)
+    want = exact(a, w)
+    try:
+        got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
+    except NotSupported as e:   # partial sums larger than the ring for this batch
+        assert "cluster size" in str(e) and m > 2, e
+        return
+    assert np.array_equal(np_(got), want)
+    for dt, code in ((torch.bfloat16, "bf16"), (torch.float32, "f32")):
+        got = w8a8_mm(a, w.t(), sa, sb, dt, bias, config=cfg)
+        assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), code)), dt
+
+
+def test_declines_narrow_tiles_for_large_batches():
+    a, w = ints((17, 2048), 1), ints((1024, 2048), 2)
+    with pytest.raises(NotSupported, match="narrow"):
+        w8a8_mm(a, w.t(), one(), one(), config=Config(128, 256, split=3, cluster=4))
 
 
 def test_declines_a_cluster_whose_partial_sums_do_not_fit():
@@ -218,8 +253,7 @@ def test_repeated_split_calls_leave_the_workspace_clean(split):
     for i, (m, k, n) in enumerate([(1, 2048, 2048), (3, 6144, 2048), (16, 2048, 12288),
                                    (1, 14336, 4096), (40, 2048, 2048), (1, 2048, 2048)] * 2):
         a, w = ints((m, k), 30 + i), ints((n, k), 40 + i)
-        cfg = default_config(m, n, k)
-        cfg = Config(cfg.bm, cfg.bn, split=split)
+        cfg = Config(tok_tile(m), 128, split=split)
         assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), exact(a, w))
     assert _native.read_status() == 0
 
@@ -234,8 +268,7 @@ def test_cluster_split_bf16_bit_exact(m, k, n, store):
     sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
     sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
-    cfg = default_config(m, n, k)
-    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=Config(cfg.bm, cfg.bn, split=3, store=store))
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=Config(tok_tile(m), 128, split=3, store=store))
     want = to_bits(og.epilogue_f32(exact(a, w), np_(sa), np_(sb), np_(bias)), "bf16")
     assert np.array_equal(bits(got), want)
 
@@ -262,7 +295,9 @@ def test_empty_batch():
 
 
 def test_choose_config_is_per_shape():
-    assert choose_config(1, 4096, 2048).swapped and not choose_config(4096, 4096, 2048).swapped
+    decode, prefill = choose_config(1, 4096, 2048), choose_config(4096, 4096, 2048)
+    assert decode.swapped or decode.split == 3   # swap_ab or narrow decode tiles
+    assert not prefill.swapped and prefill.split != 3
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
