@@ -43,8 +43,28 @@ METRIC = "W8A8 GEMM µs & roofline % per (M,K,N); stand-in decode µs/layer at b
 M_SWEEP = [1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 1024, 4096]
 QUANT_M = [1, 16, 64, 128, 1024, 4096]    # BASELINE config 3 batch sizes timed
 STANDIN_BATCHES = [1, 2, 4, 8, 16, 32, 64, 128]
-COPIES = 8          # weight copies per layer = launches per shape per step (L2-cold)
+COPIES = 8          # launches per shape per step, each on its own weight copy
 L2_BYTES = 126 << 20
+
+
+def pool_size(nbytes: int) -> int:
+    """Copies of one weight to rotate through: together at least twice the L2, in whole
+    windows of COPIES, so no launch finds its weight left in L2 by an earlier one."""
+    n = max(COPIES, -(-2 * L2_BYTES // nbytes))
+    return -(-n // COPIES) * COPIES
+
+
+_FLUSH = None
+
+
+def flush_l2():
+    """Write a buffer twice the L2's size (evicts every weight and activation)."""
+    import torch
+
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    _FLUSH.zero_()
 
 
 def parse():
@@ -160,7 +180,7 @@ def build_operands(model, world, rank, dev):
         assert n % world == 0, f"{name}: N={n} does not split over {world} GPUs"
         nl = n // world
         copies = []
-        for _ in range(COPIES):
+        for _ in range(pool_size(nl * k)):
             w = (torch.randn((nl, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
             wq, ws = quant_rows_t(w)
             del w
@@ -202,13 +222,17 @@ def capture(fn):
     return graph
 
 
-def time_graph(graph, windows=5):
+def time_graph(graph, windows=5, flush=True):
+    """Median µs of `windows` replays, L2 flushed before each (outside the timed span)
+    unless flush is False."""
     import torch
 
     graph.replay()
     torch.cuda.synchronize()
     ts = []
     for _ in range(windows):
+        if flush:
+            flush_l2()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         graph.replay()
@@ -239,10 +263,14 @@ def run_ours(args, world, rank, dev):
                 w8a8_mm(a_q, wq.t(), a_s, ws, torch.bfloat16, b)
         return fn
 
-    # per-shape graphs: COPIES launches on distinct weight copies (L2-cold)
-    graphs, per_shape = [], []
+    # per-shape graphs: COPIES launches on distinct weight copies, each case on the next
+    # window of its layer's pool (L2-cold in the timed region too, where the cases of a
+    # layer run back to back)
+    graphs, per_shape, window = [], [], {}
     for lay, m, bias in cases:
-        g = capture(launcher(lay, m, bias, lay["copies"]))
+        w0 = window.get(lay["name"], 0)
+        window[lay["name"]] = (w0 + COPIES) % len(lay["copies"])
+        g = capture(launcher(lay, m, bias, lay["copies"][w0:w0 + COPIES]))
         graphs.append(g)
     for (lay, m, bias), g in zip(cases, graphs):
         us = time_graph(g) / COPIES
@@ -260,7 +288,7 @@ def run_ours(args, world, rank, dev):
         if bias:
             continue
         g = capture(launcher(lay, m, False, [lay["copies"][0]] * COPIES))
-        warm[f"{lay['name']}/{m}"] = round(time_graph(g) / COPIES, 3)
+        warm[f"{lay['name']}/{m}"] = round(time_graph(g, flush=False) / COPIES, 3)
         del g
 
     # ------------------------------------------------ timed region
@@ -400,16 +428,19 @@ def host_cost(mm, op, fq, dev) -> dict:
     gu = torch.randn((1, 12288), device=dev).to(torch.bfloat16)
     out = {}
 
-    def t(name, fn, n=2000):
-        for _ in range(200):
-            fn()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(n):
-            fn()
-        t1 = time.perf_counter()
-        torch.cuda.synchronize()
-        out[name] = round((t1 - t0) / n * 1e6, 2)
+    def t(name, fn, n=2000, reps=3):
+        best = float("inf")
+        for _ in range(reps):    # best of `reps` runs: other host activity only adds time
+            for _ in range(200):
+                fn()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(n):
+                fn()
+            t1 = time.perf_counter()
+            torch.cuda.synchronize()
+            best = min(best, (t1 - t0) / n)
+        out[name] = round(best * 1e6, 2)
 
     t("w8a8_mm", lambda: mm(a, w.t(), sa, sb, torch.bfloat16))
     t("custom_op_w8a8_mm", lambda: op(a, w.t(), sa, sb, torch.bfloat16, None))
@@ -438,12 +469,15 @@ def run_e2e(layers, acts, cases, dev, world, passes):
     dev_bufs = {id(ha): (torch.empty_like(ha, device=dev), torch.empty_like(hs, device=dev))
                 for _, _, _, ha, hs, _ in host}
 
+    turn = {}
+
     def one_pass():
-        for i, (lay, m, bias, ha, hs, ho) in enumerate(host):
+        for lay, m, bias, ha, hs, ho in host:
             da, ds = dev_bufs[id(ha)]
             da.copy_(ha, non_blocking=True)
             ds.copy_(hs, non_blocking=True)
-            wq, ws = lay["copies"][i % COPIES]
+            i = turn[lay["name"]] = (turn.get(lay["name"], -1) + 1) % len(lay["copies"])
+            wq, ws = lay["copies"][i]
             out = w8a8_mm(da, wq.t(), ds, ws, torch.bfloat16, lay["bias"] if bias else None)
             ho.copy_(out, non_blocking=True)
 
@@ -623,16 +657,17 @@ def run_reference_triton_child(args):
     per = {}
     for name, k, n in layers_for(args.model):
         ws = [quant_rows_t((torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16))
-              for _ in range(COPIES)]
+              for _ in range(pool_size(n * k))]
+        w0 = 0
         bias = (torch.randn(n, generator=g, device=dev) * 0.01).to(torch.bfloat16)
         for m in M_SWEEP:
             a_q, a_s = quant_rows_t(torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16))
             for b in (None, bias):    # the same 96 cases as our arm: with and without bias
-                it = iter(range(1 << 40))
+                window = ws[w0:w0 + COPIES]
+                w0 = (w0 + COPIES) % len(ws)
 
-                def fn(b=b, it=it):
-                    for _ in range(COPIES):
-                        wq, wsc = ws[next(it) % COPIES]
+                def fn(b=b, window=window):
+                    for wq, wsc in window:
                         ref_mm(a_q, wq.t(), a_s, wsc, torch.bfloat16, b)
                 key = f"{name}/{m}" + ("" if b is None else "/bias")
                 per[key] = round(time_graph(capture(fn)) / COPIES, 3)
@@ -740,7 +775,9 @@ def main():
                                    f"{1 if args.model.startswith('qwen') else 2})",
                        "layers": [f"{nm} K={k} N={n}" for nm, k, n in layers_for(args.model)],
                        "M": M_SWEEP, "bias": [False, True],
-                       "l2": f"cold: {COPIES} weight copies per layer rotated, inputs > L2",
+                       "l2": (f"cold: {COPIES} launches per case on distinct weight copies from a pool of "
+                              "at least 2x L2 per layer; L2 flushed before each timed window of a "
+                              "case"),
                        "parallelism": f"column-parallel N/{world}" if world > 1 else "single GPU",
                        "pdl": not args.no_pdl}}
     if args.impl == "reference-triton":

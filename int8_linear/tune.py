@@ -1,17 +1,25 @@
 """Per-shape tile tuner for B200: writes int8_linear/tuned_configs.json.
 
     python -m int8_linear.tune [--shapes qwen3-1.7b-vllm llama-3-8b] [--m 1 2 4 ...]
-                               [--tp 1 2 4 8] [--out PATH]
+                               [--tp 1 2 4 8] [--out PATH] [--context gemm|decode]
 
 Same table format as the reference's tuned_configs.json (read by tuned_config,
 int8_linear/kernel.py):  {device name: {"KxN": {"M": {"config": {...}, "graph_us": t}}}}.
 For every (K, N, M) each candidate tiling is timed as a CUDA graph of back-to-back
-launches, each on its own copy of the weight (L2-cold, as in a decode step that streams
+launches, each on its own copy of the weight, the copies together at least twice the L2
+and the L2 flushed before each timed replay (L2-cold, as in a decode step that streams
 every layer's weights), with programmatic dependent launch on; the fastest goes into
 the table.  A candidate whose int32 product differs from the default tiling's is
 rejected (all tilings must give identical bits).  --tp N also tunes the per-GPU shards
 of a tensor-parallel split (column shards N/g of qkv and gate_up, row shards K/g of
 o_proj and down).
+
+--context decode (the default) times each candidate the way a decode step runs it: every
+GEMM follows the add+RMSNorm+quant kernel that produces its int8 activations (the time of
+that quantiser alone is subtracted).  --context gemm times GEMMs back to back.  On the
+28-layer stand-in decode step, tables tuned in decode context with L2-cold weights
+predicted the fastest tilings; tables tuned with 8 rotated copies (67 MB for a
+2048 x 4096 weight, inside the 126 MB L2) picked narrow tiles that were slower there.
 """
 
 from __future__ import annotations
@@ -24,11 +32,29 @@ from dataclasses import asdict
 import torch
 
 from int8_linear import _native
+from int8_linear import fused_quant as fq
 from int8_linear.kernel import TOKEN_TILES, TUNED_PATH, Config, NotSupported, default_config, w8a8_mm
 from int8_linear.shapes import SHAPES
 
 M_DEFAULT = [1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 1024, 4096]
-COPIES = 8
+COPIES = 8            # fewest weight copies per graph
+L2_BYTES = 126 << 20  # B200
+
+
+def pool_size(nbytes: int) -> int:
+    """Weight copies one graph rotates through: at least COPIES, and together at least
+    twice the L2, so that no launch finds its weight left in L2 by an earlier one."""
+    return max(COPIES, -(-2 * L2_BYTES // nbytes))
+
+
+_flush: torch.Tensor | None = None
+
+
+def flush_l2() -> None:
+    global _flush
+    if _flush is None:
+        _flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    _flush.zero_()
 
 
 def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
@@ -85,6 +111,7 @@ def graph_us(fn, reps: int, windows: int = 5) -> float:
     torch.cuda.synchronize()
     times = []
     for _ in range(windows):
+        flush_l2()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         graph.replay()
@@ -95,10 +122,12 @@ def graph_us(fn, reps: int, windows: int = 5) -> float:
     return statistics.median(times)
 
 
-def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True) -> dict:
+def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True,
+               context: str = "gemm") -> dict:
     g = torch.Generator(device="cuda").manual_seed(k * 31 + n)
+    copies = pool_size(n * k)
     ws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
-          for _ in range(COPIES)]
+          for _ in range(copies)]
     sb = torch.rand((n, 1), device="cuda", generator=g) * 1e-3 + 1e-4
     one = torch.ones(1, device="cuda")
     table = {}
@@ -106,6 +135,11 @@ def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True) ->
         a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
         sa = torch.rand((m, 1), device="cuda", generator=g) * 1e-2 + 1e-3
         want = w8a8_mm(a, ws[0].t(), one, one, raw=True, config=default_config(m, n, k))
+        x = torch.randn((m, k), device="cuda", generator=g).to(torch.bfloat16)
+        gamma = torch.ones(k, device="cuda", dtype=torch.bfloat16)
+        base = 0.0
+        if context == "decode":
+            base = graph_us(lambda: fq.add_rmsnorm_quant(x, None, gamma, 1e-6), copies)
         best = None
         for cfg in candidates(m, n, k, sms):
             try:
@@ -117,9 +151,13 @@ def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True) ->
             it = iter(range(1 << 40))
 
             def fn(cfg=cfg, it=it):
-                w8a8_mm(a, ws[next(it) % COPIES].t(), sa, sb, torch.bfloat16, config=cfg)
+                if context == "decode":
+                    q, s, _ = fq.add_rmsnorm_quant(x, None, gamma, 1e-6)
+                    w8a8_mm(q, ws[next(it) % copies].t(), s, sb, torch.bfloat16, config=cfg)
+                else:
+                    w8a8_mm(a, ws[next(it) % copies].t(), sa, sb, torch.bfloat16, config=cfg)
 
-            us = graph_us(fn, COPIES)
+            us = graph_us(fn, copies) - base
             if best is None or us < best[1]:
                 best = (cfg, us)
         assert best is not None
@@ -147,6 +185,8 @@ def main() -> None:
     ap.add_argument("--m", nargs="*", type=int, default=M_DEFAULT)
     ap.add_argument("--tp", nargs="*", type=int, default=[1])
     ap.add_argument("--out", default=str(TUNED_PATH))
+    ap.add_argument("--context", choices=["gemm", "decode"], default="decode",
+                    help="time GEMMs back to back, or each after its activation quantiser")
     args = ap.parse_args()
     _native.set_pdl(True)
     dev = torch.cuda.get_device_name()
@@ -164,7 +204,7 @@ def main() -> None:
                 if (k, n) in done:
                     continue
                 done.add((k, n))
-                table.setdefault(f"{k}x{n}", {}).update(tune_shape(k, n, args.m, sms))
+                table.setdefault(f"{k}x{n}", {}).update(tune_shape(k, n, args.m, sms, context=args.context))
                 with open(args.out, "w") as f:
                     json.dump(tables, f, indent=1, sort_keys=True)
                     f.write("\n")
