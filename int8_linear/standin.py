@@ -19,7 +19,7 @@ from dataclasses import dataclass
 import torch
 
 from int8_linear.fused_quant import add_rmsnorm_quant, per_token_quant, silu_mul_quant
-from int8_linear.kernel import w8a8_mm
+from int8_linear.kernel import Config, w8a8_mm
 
 HIDDEN, INTER, EPS, LAYERS = 2048, 6144, 1e-6, 28
 # (K, N) of each linear, as vLLM runs Qwen3-1.7B (merged qkv and gate_up).
@@ -49,19 +49,25 @@ def make_layers(layers: int = LAYERS, seed: int = 0, device="cuda", shapes=SHAPE
 
 
 class StandinDecoder:
-    """The reference's fused stand-in step for a decode batch of m tokens."""
+    """The reference's fused stand-in step for a decode batch of m tokens.
+
+    `configs` maps a linear's name (a key of SHAPES) to the tiling its GEMMs use in every
+    layer; linears not named use the library's choice (choose_config).  It may be changed
+    between captures (the in-situ tuner does)."""
 
     def __init__(self, m: int, layers: int = LAYERS, seed: int = 0, device="cuda",
-                 norm_weight: torch.Tensor | None = None):
+                 norm_weight: torch.Tensor | None = None, configs: dict[str, Config] | None = None):
         g = torch.Generator(device=device).manual_seed(seed)
         self.x = torch.randn((m, HIDDEN), generator=g, device=device).to(torch.bfloat16)
         self.w = (norm_weight if norm_weight is not None
                   else torch.ones(HIDDEN, device=device, dtype=torch.bfloat16))
         self.layers = make_layers(layers, device=device, generator=g)
+        self.configs: dict[str, Config] = dict(configs or {})
         self.graph: torch.cuda.CUDAGraph | None = None
         self.out: torch.Tensor | None = None
 
     def step(self) -> torch.Tensor:
+        cfg = self.configs.get
         res = self.x
         q, s, _ = add_rmsnorm_quant(self.x, None, self.w, EPS)
         h = None
@@ -69,20 +75,22 @@ class StandinDecoder:
             if i:
                 q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
             lin = layer["qkv_proj"]
-            qkv = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+            qkv = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("qkv_proj"))
             q, s = per_token_quant(qkv[:, :HIDDEN])
             lin = layer["o_proj"]
-            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("o_proj"))
             q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
             lin = layer["gate_up_proj"]
-            gu = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+            gu = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("gate_up_proj"))
             q, s = silu_mul_quant(gu)
             lin = layer["down_proj"]
-            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16)
+            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("down_proj"))
         return h
 
     def capture(self) -> torch.cuda.CUDAGraph:
-        """Capture one step into a CUDA graph (after a warm-up call on a side stream)."""
+        """Capture one step into a CUDA graph (after a warm-up call on a side stream),
+        replacing any earlier capture."""
+        self.graph = None
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):

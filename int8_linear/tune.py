@@ -122,15 +122,16 @@ def graph_us(fn, reps: int, windows: int = 5) -> float:
     return statistics.median(times)
 
 
-def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True,
-               context: str = "gemm") -> dict:
+def rank_shape(k: int, n: int, ms: list[int], sms: int, context: str = "gemm") -> dict[int, list]:
+    """Every valid candidate tiling of each batch size M, fastest first: {M: [(Config,
+    µs), ...]}.  A candidate whose int32 product differs from the default tiling's raises."""
     g = torch.Generator(device="cuda").manual_seed(k * 31 + n)
     copies = pool_size(n * k)
     ws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
           for _ in range(copies)]
     sb = torch.rand((n, 1), device="cuda", generator=g) * 1e-3 + 1e-4
     one = torch.ones(1, device="cuda")
-    table = {}
+    ranked = {}
     for m in ms:
         a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
         sa = torch.rand((m, 1), device="cuda", generator=g) * 1e-2 + 1e-3
@@ -140,7 +141,7 @@ def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True,
         base = 0.0
         if context == "decode":
             base = graph_us(lambda: fq.add_rmsnorm_quant(x, None, gamma, 1e-6), copies)
-        best = None
+        timed = []
         for cfg in candidates(m, n, k, sms):
             try:
                 got = w8a8_mm(a, ws[0].t(), one, one, raw=True, config=cfg)
@@ -157,16 +158,23 @@ def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True,
                 else:
                     w8a8_mm(a, ws[next(it) % copies].t(), sa, sb, torch.bfloat16, config=cfg)
 
-            us = graph_us(fn, copies) - base
-            if best is None or us < best[1]:
-                best = (cfg, us)
-        assert best is not None
-        cfg, us = best
+            timed.append((cfg, graph_us(fn, copies) - base))
+        assert timed, f"no candidate tiling runs {m}x{k}x{n}"
+        ranked[m] = sorted(timed, key=lambda t: t[1])
+    del ws
+    torch.cuda.empty_cache()
+    return ranked
+
+
+def tune_shape(k: int, n: int, ms: list[int], sms: int, verbose: bool = True,
+               context: str = "gemm") -> dict:
+    """The table entries {"M": {"config", "graph_us"}} of one (K, N): the fastest candidate."""
+    table = {}
+    for m, timed in rank_shape(k, n, ms, sms, context).items():
+        cfg, us = timed[0]
         table[str(m)] = {"config": asdict(cfg), "graph_us": round(us, 3)}
         if verbose:
             print(f"K={k:6d} N={n:6d} M={m:5d}: {cfg.name:40s} {us:9.2f} us", flush=True)
-    del ws
-    torch.cuda.empty_cache()
     return table
 
 

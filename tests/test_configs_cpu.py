@@ -37,6 +37,6 @@ def test_tuned_table_entries_are_valid_tilings():
                 cfg.check()
                 if cfg.split == 3 and not cfg.swapped:   # narrow tiles take <= 16 tokens
                     assert int(m) <= 16, (shape, m)
-                assert entry["graph_us"] > 0
+                assert entry.get("graph_us", entry.get("stand_in_us", 0)) > 0
                 count += 1
     assert count > 0
