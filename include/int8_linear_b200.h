@@ -105,6 +105,31 @@ int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
                 size_t ws_bytes, void *stream);
 
 /*
+ * i8l_w8a8_mm with the activation's per-token quantisation fused into the GEMM:
+ * X is the bf16 (x_dtype I8L_BF16) or fp16 (I8L_F16) activation [M,K], rows ldx
+ * elements apart, 16-byte aligned.  The kernel quantises each token row as the plain
+ * per-token quantiser does (scale = absmax/127, q = rint(x * 127/absmax) saturated to
+ * [-128, 127], absmax over all K; precise_div = 1 for IEEE division, 0 for Triton's
+ * full-range division) and multiplies; the result equals i8l_quant_rows followed by
+ * i8l_w8a8_mm bit for bit, with one launch instead of two and no int8 copy of X in
+ * HBM.  Other arguments as i8l_w8a8_mm (there is no sa).
+ *
+ * Only tiles that use direct activation loads take it: swap_ab, M <= tok_tile, one
+ * tile or cluster segment per CTA, at most `stages` k-blocks per CTA (tile->act 0 or
+ * 2); any other returns I8L_ENOTSUP and the caller quantises separately.
+ *
+ * Replaces the reference's o_proj input path, vLLM's scaled_int8_quant followed by
+ * w8a8_mm (bench/fuse_quant.py:234, int8_linear/vllm_fuse_patch.py:13-14, where the
+ * reference notes that o_proj still quantises its own input).
+ */
+int i8l_w8a8_mm_quant_act(const void *X, int32_t x_dtype, int64_t ldx, int32_t precise_div,
+                          const int8_t *W, int64_t ldw, const float *sb,
+                          int32_t sb_per_col, const void *bias, int32_t bias_dtype,
+                          void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
+                          int32_t K, const i8l_tile *tile, void *workspace,
+                          size_t ws_bytes, void *stream);
+
+/*
  * i8l_w8a8_mm for callers that cannot allocate device memory.  No counterpart in
  * the reference (its Triton kernel needed no scratch).
  *

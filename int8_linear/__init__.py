@@ -11,7 +11,7 @@ one finishes and GEMMs prefetch their weight tiles meanwhile.
 """
 
 from int8_linear._native import pdl_enabled, set_pdl
-from int8_linear.kernel import Config, NotSupported, default_config, tuned_config, w8a8_mm
+from int8_linear.kernel import Config, NotSupported, default_config, tuned_config, w8a8_mm, w8a8_mm_quant_act
 
-__all__ = ["Config", "NotSupported", "default_config", "tuned_config", "w8a8_mm", "set_pdl",
-           "pdl_enabled"]
+__all__ = ["Config", "NotSupported", "default_config", "tuned_config", "w8a8_mm", "w8a8_mm_quant_act",
+           "set_pdl", "pdl_enabled"]

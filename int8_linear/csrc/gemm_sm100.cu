@@ -72,6 +72,15 @@ struct GemmArgs {
   int act_direct;
   const int8_t *act;
   long long lda;
+  // Per-token quantisation fused into the direct activation loads: act_src holds the
+  // bf16/fp16 activation (act_src_dtype, rows act_ld elements apart); the loader finds
+  // each token's absmax over all K, quantises its k-blocks as the row quantiser does
+  // (scale = absmax/127, q = rint(x * 127/absmax)), and the epilogue uses those scales.
+  int act_quant;
+  int act_src_dtype;
+  int act_precise;
+  const void *act_src;
+  long long act_ld;
   // CTA pairs (cta_group::2): the two CTAs of each 2-CTA cluster compute one tile of
   // 256 X rows (tiles_x counts 256-row tiles) x TN Y rows; each loads 128 X rows and
   // TN/2 Y rows per k-block, the even CTA issues the 256-row MMAs.  Whole tiles only.
@@ -545,6 +554,106 @@ __device__ __forceinline__ void load_act_direct(const GemmArgs &a, uint8_t *sy, 
   }
 }
 
+// Value j (0..7) of 8 bf16 or fp16 values packed in a uint4, as float (exact).
+__device__ __forceinline__ float act_val(const uint4 &v, int j, int f16) {
+  const uint32_t w = (&v.x)[j >> 1];
+  const uint32_t h = (j & 1) ? (w >> 16) : (w & 0xffffu);
+  return f16 ? __half2float(__ushort_as_half(static_cast<unsigned short>(h))) : __uint_as_float(h << 16);
+}
+
+// Direct activation loads with per-token quantisation (a.act_quant): first each token
+// row's absmax over all K (all epilogue threads, 32-byte units), giving its scale and
+// reciprocal exactly as the row quantiser computes them (scale = absmax/127, inv =
+// 127/absmax or 0, by IEEE or Triton's full-range division); then k-blocks kb0..kb1-1
+// quantised, q = rint(x * inv) saturated to [-128, 127], into the Y slots in the
+// layout load_act_direct writes.  Rows past M are zero.  All epilogue warps take part
+// (named barrier 3 between the steps).
+template <int TN>
+__device__ __forceinline__ void load_act_quant(const GemmArgs &a, uint8_t *sy, int kb0, int kb1,
+                                               int tid, float *act_scale, float *act_inv) {
+  constexpr int kChunks = TN * (kBK / 16);
+  constexpr int kThr = kEpiWarps * 32;
+  const int f16 = a.act_src_dtype == I8L_F16;
+  const uint8_t *src = static_cast<const uint8_t *>(a.act_src);
+  const long long ld_bytes = a.act_ld * 2;
+  // Row absmax: units of 16 values (32 bytes) over all rows, 8 per thread in flight;
+  // each unit's max (fmaxf from 0, so NaN is ignored as the row quantiser ignores it)
+  // goes into the row's slot with an integer atomicMax, exact for non-negative floats.
+  int *amax_bits = reinterpret_cast<int *>(act_inv);
+  for (int r = tid; r < TN; r += kThr) amax_bits[r] = 0;
+  named_bar_sync(3, kThr);
+  const int cpr = a.K / 16;  // units per row (K is a multiple of 16)
+  const int units = min(a.M, TN) * cpr;
+  for (int u0 = tid; u0 < units; u0 += 8 * kThr) {
+    uint4 q[8][2];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int id = u0 + u * kThr;
+      q[u][0] = q[u][1] = make_uint4(0u, 0u, 0u, 0u);
+      if (id < units) {
+        const int8_t *p = reinterpret_cast<const int8_t *>(src + (id / cpr) * ld_bytes + (id % cpr) * 32);
+        q[u][0] = ld_cg_v4(p);
+        q[u][1] = ld_cg_v4(p + 16);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int id = u0 + u * kThr;
+      if (id < units) {
+        float mx = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) mx = fmaxf(mx, fabsf(act_val(q[u][e >> 3], e & 7, f16)));
+        atomicMax(&amax_bits[id / cpr], __float_as_int(mx));
+      }
+    }
+  }
+  named_bar_sync(3, kThr);
+  for (int r = tid; r < a.M && r < TN; r += kThr) {
+    const float amax = __int_as_float(amax_bits[r]);
+    act_scale[r] = a.act_precise ? div_rn(amax, 127.f) : div_full(amax, 127.f);
+    act_inv[r] = amax == 0.f ? 0.f : (a.act_precise ? div_rn(127.f, amax) : div_full(127.f, amax));
+  }
+  named_bar_sync(3, kThr);
+  const int n = (kb1 - kb0) * kChunks;
+  for (int base = tid; base < n; base += 4 * kThr) {
+    uint4 v[4][2];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int id = base + u * kThr;
+      v[u][0] = v[u][1] = make_uint4(0u, 0u, 0u, 0u);
+      if (id < n) {
+        const int j = id / kChunks, r = (id % kChunks) >> 3, c = id & 7;
+        const long long col = static_cast<long long>(kb0 + j) * kBK + c * 16;
+        if (r < a.M && col < a.K) {
+          const int8_t *p = reinterpret_cast<const int8_t *>(src + r * ld_bytes + col * 2);
+          v[u][0] = ld_cg_v4(p);
+          v[u][1] = ld_cg_v4(p + 16);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int id = base + u * kThr;
+      if (id < n) {
+        const int j = id / kChunks, r = (id % kChunks) >> 3, c = id & 7;
+        uint32_t packed[4] = {0u, 0u, 0u, 0u};
+        if (r < a.M) {
+          const float inv = act_inv[r];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            int q = __float2int_rn(__fmul_rn(act_val(v[u][e >> 3], e & 7, f16), inv));
+            q = q < -128 ? -128 : (q > 127 ? 127 : q);
+            packed[e >> 2] |= (static_cast<uint32_t>(q) & 0xffu) << ((e & 3) * 8);
+          }
+        }
+        *reinterpret_cast<uint4 *>(sy + static_cast<size_t>(j) * (TN * kBK) + r * kBK +
+                                   ((c ^ (r & 7)) << 4)) =
+            make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      }
+    }
+  }
+}
+
 // Decode tiles (TN <= 64) cap registers so two CTAs fit on an SM: with programmatic
 // dependent launch the next GEMM's CTA streams its weights beside this one.
 template <int TN, int kVar>
@@ -840,7 +949,13 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
     if (a.act_direct) {
       Schedule s0 = sch;
       Segment g0;
-      if (s0.next(a, g0)) load_act_direct<TN>(a, sy, g0.kb0, g0.kb1, epi_tid);
+      if (s0.next(a, g0)) {
+        if (a.act_quant)
+          load_act_quant<TN>(a, sy, g0.kb0, g0.kb1, epi_tid, scal + 2 * kScalFloats,
+                             scal + 3 * kScalFloats);
+        else
+          load_act_direct<TN>(a, sy, g0.kb0, g0.kb1, epi_tid);
+      }
       fence_proxy_async_smem();  // generic-proxy stores -> operands of tcgen05.mma
       __syncwarp();
       if (lane == 0) mbar_arrive(act_bar);
@@ -871,9 +986,13 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
             t.s_row = a.sb_per_col ? a.sb[n] : a.sb[0];
             t.b_row = has_bias ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f;
           }
+          // (fused activation quantisation: the loader's scales, in the b_col area,
+          // which swap tiles do not use)
           for (int c = epi_tid; c < TN; c += kEpiWarps * 32) {
             const int m = t.ty * TN + c;
-            s_col[c] = m < a.M ? (a.sa_per_row ? a.sa[m] : a.sa[0]) : 0.f;
+            s_col[c] = m < a.M ? (a.act_quant ? scal[2 * kScalFloats + m]
+                                              : (a.sa_per_row ? a.sa[m] : a.sa[0]))
+                               : 0.f;
           }
         } else {
           const int m = t.tx * kXRows + row;
@@ -1503,11 +1622,23 @@ extern "C" size_t i8l_workspace_size(int32_t M, int32_t N, int32_t K, const i8l_
   return p.ws_bytes;
 }
 
-extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
-                           const float *sa, int32_t sa_per_row, const float *sb,
-                           int32_t sb_per_col, const void *bias, int32_t bias_dtype, void *out,
-                           int32_t out_dtype, int64_t ldc, int32_t M, int32_t N, int32_t K,
-                           const i8l_tile *tile, void *workspace, size_t ws_bytes, void *stream) {
+namespace i8l {
+
+// A bf16/fp16 activation quantised per token inside the GEMM (i8l_w8a8_mm_quant_act).
+struct ActQuant {
+  const void *x;
+  int dtype;  // I8L_BF16 or I8L_F16
+  int64_t ldx;  // elements
+  int precise;
+};
+
+// The body of i8l_w8a8_mm and i8l_w8a8_mm_quant_act.  With aq, A is aq->x (read only
+// by the kernel's direct activation loads; the tile must allow them).
+static int gemm_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, const float *sa,
+                    int32_t sa_per_row, const float *sb, int32_t sb_per_col, const void *bias,
+                    int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldc, int32_t M,
+                    int32_t N, int32_t K, const i8l_tile *tile, void *workspace, size_t ws_bytes,
+                    void *stream, const ActQuant *aq) {
   if (M < 0 || N < 0 || K < 0) return set_error(I8L_EINVAL, "negative size M=%d N=%d K=%d", M, N, K);
   if (out_dtype < I8L_BF16 || out_dtype > I8L_I32)
     return set_error(I8L_ENOTSUP, "output dtype code %d not supported", out_dtype);
@@ -1523,13 +1654,18 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
     return set_error(I8L_ENOTSUP, "int8 operands and their row strides must be 16-byte aligned");
   const bool raw = out_dtype == I8L_I32;
   if (!raw) {
-    if (!sa || !sb) return set_error(I8L_EINVAL, "NULL scale pointer");
+    if ((!sa && !aq) || !sb) return set_error(I8L_EINVAL, "NULL scale pointer");
     if (bias && (bias_dtype < I8L_BF16 || bias_dtype > I8L_F32))
       return set_error(I8L_ENOTSUP, "bias dtype code %d not supported", bias_dtype);
   }
   Plan p;
   int e = make_plan(M, N, K, tile, &p);
   if (e) return e;
+  if (aq && p.tile.act != 2)
+    return set_error(I8L_ENOTSUP,
+                     "fused activation quantisation needs direct activation loads: swap_ab, "
+                     "M <= tok_tile, one tile or cluster segment per CTA and at most `stages` "
+                     "k-blocks per CTA");
   if (p.ws_bytes > 0 && (workspace == nullptr || ws_bytes < p.ws_bytes))
     return set_error(I8L_EWORKSPACE, "workspace of %zu bytes needed, %zu given", p.ws_bytes,
                      workspace ? ws_bytes : static_cast<size_t>(0));
@@ -1605,6 +1741,13 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
   a.pair = p.pair;
   a.act = A;
   a.lda = lda;
+  if (aq) {
+    a.act_quant = 1;
+    a.act_src_dtype = aq->dtype;
+    a.act_precise = aq->precise ? 1 : 0;
+    a.act_src = aq->x;
+    a.act_ld = aq->ldx;
+  }
   // Early cluster mode needs the (cluster-1) slots, each TN x 128 int32 apart, inside
   // the leader's staging area, which plain stores leave unused.
   if (p.cluster > 1 && !a.tma_out) {
@@ -1629,6 +1772,38 @@ extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_
     default:
       return set_error(I8L_ENOTSUP, "no kernel for tile width %d", p.tn);
   }
+}
+
+}  // namespace i8l
+
+extern "C" int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
+                           const float *sa, int32_t sa_per_row, const float *sb,
+                           int32_t sb_per_col, const void *bias, int32_t bias_dtype, void *out,
+                           int32_t out_dtype, int64_t ldc, int32_t M, int32_t N, int32_t K,
+                           const i8l_tile *tile, void *workspace, size_t ws_bytes, void *stream) {
+  return gemm_run(A, lda, W, ldw, sa, sa_per_row, sb, sb_per_col, bias, bias_dtype, out, out_dtype,
+                  ldc, M, N, K, tile, workspace, ws_bytes, stream, nullptr);
+}
+
+extern "C" int i8l_w8a8_mm_quant_act(const void *X, int32_t x_dtype, int64_t ldx, int32_t precise_div,
+                                     const int8_t *W, int64_t ldw, const float *sb,
+                                     int32_t sb_per_col, const void *bias, int32_t bias_dtype,
+                                     void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
+                                     int32_t K, const i8l_tile *tile, void *workspace,
+                                     size_t ws_bytes, void *stream) {
+  if (x_dtype != I8L_BF16 && x_dtype != I8L_F16)
+    return set_error(I8L_ENOTSUP, "activation dtype code %d not supported (bf16 or fp16)", x_dtype);
+  if (M > 0 && N > 0 && K > 0) {
+    if (!X) return set_error(I8L_EINVAL, "NULL activation pointer");
+    if (ldx < K) return set_error(I8L_EINVAL, "activation row stride %lld < K=%d", static_cast<long long>(ldx), K);
+    if (reinterpret_cast<uintptr_t>(X) % 16 || (ldx * 2) % 16)
+      return set_error(I8L_ENOTSUP, "the activation and its row stride must be 16-byte aligned");
+  }
+  const ActQuant aq{X, x_dtype, ldx, precise_div};
+  // The int8 A pointer and stride stand in for X's bytes: only the direct loads read A,
+  // and through aq.  (X's rows are 2*ldx bytes apart and hold at least K bytes.)
+  return gemm_run(static_cast<const int8_t *>(X), ldx * 2, W, ldw, nullptr, 0, sb, sb_per_col, bias,
+                  bias_dtype, out, out_dtype, ldc, M, N, K, tile, workspace, ws_bytes, stream, &aq);
 }
 
 // ------------------------------------------------------------------ no-allocation entry

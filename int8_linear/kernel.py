@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import ctypes
 import json
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 from functools import lru_cache
 from pathlib import Path
 
@@ -36,7 +36,8 @@ TOKEN_TILES = (16, 32, 64, 128, 256)
 # 148 SMs, so one allocation covers every call.
 WORKSPACE_BYTES = 32 << 20
 
-__all__ = ["Config", "NotSupported", "default_config", "tuned_config", "choose_config", "w8a8_mm"]
+__all__ = ["Config", "NotSupported", "default_config", "tuned_config", "choose_config", "w8a8_mm",
+           "w8a8_mm_quant_act"]
 
 
 @dataclass(frozen=True)
@@ -302,6 +303,108 @@ def _launch(lib, a, wp, ldw, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, w
         _DTYPE_CODE[bias.dtype] if bias is not None else 0,
         out.data_ptr(), _native.I32 if raw else _DTYPE_CODE[out_dtype], out.stride(0),
         m, n, k, ctypes.byref(tile), ws.data_ptr(), ws.numel(), stream)
+
+
+def fused_act_config(cfg: Config) -> Config | None:
+    """The tiling of cfg with direct activation loads (which the fused activation
+    quantisation rides on), or None when cfg is not a swap_ab tile."""
+    if not cfg.swapped:
+        return None
+    return cfg if cfg.act == 2 else replace(cfg, act=2)
+
+
+def _fused_candidates(m: int, n: int, k: int) -> list[Config]:
+    """Tilings w8a8_mm_quant_act tries, in order, when the caller names none: the
+    table's (with direct loads), then cluster split-K tilings of the smallest token tile
+    that holds M, then whole tiles, one per CTA."""
+    out = []
+    base = fused_act_config(choose_config(m, n, k))
+    if base is not None:
+        out.append(base)
+    if m <= 64:
+        tn = next(t for t in TOKEN_TILES if t >= m)
+        out += [Config(tn, 128, split=3, cluster=c, act=2) for c in (4, 8, 3, 2, 6)]
+        out.append(Config(tn, 128, split=1, act=2, ctas=-(-n // 128)))
+    return out
+
+
+_fused_chosen: dict[tuple[int, int, int, int], Config | None] = {}
+
+
+def w8a8_mm_quant_act(
+    x: torch.Tensor,
+    b_q: torch.Tensor,
+    scale_b: torch.Tensor,
+    out_dtype: torch.dtype = torch.bfloat16,
+    bias: torch.Tensor | None = None,
+    *,
+    config: Config | None = None,
+    precise_div: bool = True,
+    raw: bool = False,
+) -> torch.Tensor:
+    """w8a8_mm of x's dynamic per-token int8 quantisation: the same bits as
+    `q, s = fused_quant.per_token_quant(x, precise_div); w8a8_mm(q, b_q, s, scale_b, ...)`.
+
+    x is a bf16/fp16 [M, K] activation with contiguous, 16-byte aligned rows (a column
+    slice of a wider matrix is fine).  Where a tiling with direct activation loads takes
+    the problem (decode batches on swap_ab tiles), one kernel quantises x while loading
+    it; otherwise the two steps above run.  With config=None the first of the table's
+    tiling and a few cluster split-K tilings that the library accepts is used (and
+    remembered per shape).  This is the reference's o_proj input path
+    (bench/fuse_quant.py:234: vLLM's scaled_int8_quant, then w8a8_mm) in one launch.
+    """
+    if x.dtype not in (torch.bfloat16, torch.float16) or x.dim() != 2 or x.stride(1) != 1:
+        raise NotSupported("x must be a 2-D bf16/fp16 activation with contiguous rows")
+    if b_q.dtype != torch.int8 or b_q.dim() != 2 or x.shape[1] != b_q.shape[0]:
+        raise ValueError(f"cannot multiply {tuple(x.shape)} by {tuple(b_q.shape)}")
+    m, k = x.shape
+    n = b_q.shape[1]
+    fusable = (m > 0 and n > 0 and k % 16 == 0 and x.is_cuda and x.data_ptr() % 16 == 0
+               and (x.stride(0) * 2) % 16 == 0 and b_q.stride(0) == 1 and b_q.data_ptr() % 16 == 0
+               and b_q.stride(1) % 16 == 0)
+    if fusable:
+        sb = scale_b if scale_b.is_contiguous() else scale_b.contiguous()
+        if sb.dtype != torch.float32 or sb.numel() not in (1, n):
+            raise ValueError(f"scale_b must hold 1 or {n} float32 values")
+        if bias is not None:
+            if tuple(bias.shape) != (n,):
+                raise ValueError(f"bias must have shape ({n},), got {tuple(bias.shape)}")
+            if bias.dtype not in _DTYPE_CODE:
+                raise NotSupported(f"bias dtype {bias.dtype} not supported")
+            bias = bias.contiguous()
+        if not raw and out_dtype not in _DTYPE_CODE:
+            raise NotSupported(f"output dtype {out_dtype} not supported")
+        dev = x.get_device()
+        key = (dev, m, n, k)
+        if config is not None:
+            tries = [c for c in (fused_act_config(config),) if c is not None]
+        elif key in _fused_chosen:
+            tries = [c for c in (_fused_chosen[key],) if c is not None]
+        else:
+            tries = _fused_candidates(m, n, k)
+        out = torch.empty((m, n), dtype=torch.int32 if raw else out_dtype, device=x.device)
+        lib = _native.load()
+        stream = current_stream(dev)
+        ws = workspace(dev, stream)
+        for cfg in tries:
+            code = lib.i8l_w8a8_mm_quant_act(
+                x.data_ptr(), _native.BF16 if x.dtype == torch.bfloat16 else _native.F16,
+                x.stride(0), int(bool(precise_div)), b_q.data_ptr(), b_q.stride(1), sb.data_ptr(),
+                int(sb.numel() > 1), bias.data_ptr() if bias is not None else None,
+                _DTYPE_CODE[bias.dtype] if bias is not None else 0,
+                out.data_ptr(), _native.I32 if raw else _DTYPE_CODE[out_dtype], out.stride(0),
+                m, n, k, ctypes.byref(_tile_of(cfg)), ws.data_ptr(), ws.numel(), stream)
+            if code != _native.ENOTSUP:
+                _native.check(code)
+                if config is None:
+                    _fused_chosen[key] = cfg
+                return out
+        if config is None:
+            _fused_chosen[key] = None
+    from int8_linear.fused_quant import per_token_quant
+
+    q, s = per_token_quant(x, precise_div)
+    return w8a8_mm(q, b_q, s, scale_b, out_dtype, bias, config=config, raw=raw)
 
 
 def dequant_i32(acc: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,

@@ -9,7 +9,12 @@ step runs, per layer,
 
 captured as one CUDA graph.  Here the qkv slice is quantised in place (the quantiser
 reads rows with a stride), where the reference copies it with .contiguous() and then
-calls vLLM's scaled_int8_quant; the values are the same.
+calls vLLM's scaled_int8_quant; the values are the same.  With fuse_o_proj that
+quantiser runs inside the o_proj GEMM (w8a8_mm_quant_act) wherever a tiling with direct
+activation loads takes the batch: one launch fewer per layer, the same bits.  It is off
+by default: on B200 the fused GEMM was measured slower than the quantiser followed by
+the tuned tiling (the tilings that take direct loads are slower at these shapes, and
+the fused loads add a dependent round trip for the row absmax).
 """
 
 from __future__ import annotations
@@ -19,7 +24,8 @@ from dataclasses import dataclass
 import torch
 
 from int8_linear.fused_quant import add_rmsnorm_quant, per_token_quant, silu_mul_quant
-from int8_linear.kernel import Config, w8a8_mm
+from int8_linear import kernel
+from int8_linear.kernel import Config, w8a8_mm, w8a8_mm_quant_act
 
 HIDDEN, INTER, EPS, LAYERS = 2048, 6144, 1e-6, 28
 # (K, N) of each linear, as vLLM runs Qwen3-1.7B (merged qkv and gate_up).
@@ -56,13 +62,15 @@ class StandinDecoder:
     between captures (the in-situ tuner does)."""
 
     def __init__(self, m: int, layers: int = LAYERS, seed: int = 0, device="cuda",
-                 norm_weight: torch.Tensor | None = None, configs: dict[str, Config] | None = None):
+                 norm_weight: torch.Tensor | None = None, configs: dict[str, Config] | None = None,
+                 fuse_o_proj: bool = False):
         g = torch.Generator(device=device).manual_seed(seed)
         self.x = torch.randn((m, HIDDEN), generator=g, device=device).to(torch.bfloat16)
         self.w = (norm_weight if norm_weight is not None
                   else torch.ones(HIDDEN, device=device, dtype=torch.bfloat16))
         self.layers = make_layers(layers, device=device, generator=g)
         self.configs: dict[str, Config] = dict(configs or {})
+        self.fuse_o_proj = fuse_o_proj
         self.graph: torch.cuda.CUDAGraph | None = None
         self.out: torch.Tensor | None = None
 
@@ -76,9 +84,13 @@ class StandinDecoder:
                 q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
             lin = layer["qkv_proj"]
             qkv = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("qkv_proj"))
-            q, s = per_token_quant(qkv[:, :HIDDEN])
             lin = layer["o_proj"]
-            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("o_proj"))
+            if self.fuse_o_proj:
+                h = w8a8_mm_quant_act(qkv[:, :HIDDEN], lin.w_t, lin.scale, torch.bfloat16,
+                                      config=cfg("o_proj"))
+            else:
+                q, s = per_token_quant(qkv[:, :HIDDEN])
+                h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("o_proj"))
             q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
             lin = layer["gate_up_proj"]
             gu = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("gate_up_proj"))
@@ -101,9 +113,20 @@ class StandinDecoder:
             self.out = self.step()
         return self.graph
 
+    def o_proj_fused(self) -> bool:
+        """Whether o_proj's input quantisation runs inside its GEMM at this batch."""
+        if not self.fuse_o_proj:
+            return False
+        m = self.x.shape[0]
+        k, n = SHAPES["o_proj"]
+        if self.configs.get("o_proj") is not None:
+            return kernel.fused_act_config(self.configs["o_proj"]) is not None
+        return kernel._fused_chosen.get((self.x.get_device(), m, n, k)) is not None
+
     @property
     def launches_per_step(self) -> int:
-        return 1 + len(self.layers) * 7 + (len(self.layers) - 1)
+        per_layer = 6 if self.o_proj_fused() else 7
+        return 1 + len(self.layers) * per_layer + (len(self.layers) - 1)
 
     def weight_bytes(self) -> int:
         return sum(lin.w_t.numel() + lin.scale.numel() * 4 for layer in self.layers
