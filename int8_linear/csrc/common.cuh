@@ -466,4 +466,39 @@ __device__ __forceinline__ float round_through(float v) {
   return ActType<DT>::to_f32(ActType<DT>::from_f32(v));
 }
 
+// Two fp32 products / sums in one sm_100 instruction (.f32x2): each lane is the IEEE
+// round-to-nearest result __fmul_rn / __fadd_rn gives, never contracted into an FMA.
+__device__ __forceinline__ void mul2_rn(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n.reg .b64 ra, rb, rd;\n"
+      "mov.b64 ra, {%2, %3};\n"
+      "mov.b64 rb, {%4, %5};\n"
+      "mul.rn.f32x2 rd, ra, rb;\n"
+      "mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void add2_rn(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n.reg .b64 ra, rb, rd;\n"
+      "mov.b64 ra, {%2, %3};\n"
+      "mov.b64 rb, {%4, %5};\n"
+      "add.rn.f32x2 rd, ra, rb;\n"
+      "mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// Round two fp32 values through bf16 (one cvt.rn.bf16x2) or fp16 and back.
+template <int DT>
+__device__ __forceinline__ void round2_through(float &v0, float &v1) {
+  if constexpr (DT == I8L_BF16) {
+    uint32_t p;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v1), "f"(v0));
+    v0 = __uint_as_float(p << 16);
+    v1 = __uint_as_float(p & 0xffff0000u);
+  } else if constexpr (DT == I8L_F16) {
+    v0 = round_through<I8L_F16>(v0);
+    v1 = round_through<I8L_F16>(v1);
+  }
+}
+
 }  // namespace i8l

@@ -64,8 +64,14 @@ __global__ void __launch_bounds__(row_max_threads(NV, VW)) add_rmsnorm_quant_ker
       if (a.res) {
         float r[VW];
         load_vec<DT, VW>(static_cast<const T *>(a.res) + row * a.ldr, col, r);
+        if constexpr (VW % 2 == 0) {
 #pragma unroll
-        for (int i = 0; i < VW; ++i) x[v][i] = __fadd_rn(x[v][i], r[i]);
+          for (int i = 0; i < VW; i += 2)
+            add2_rn(x[v][i], x[v][i + 1], x[v][i], x[v][i + 1], r[i], r[i + 1]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VW; ++i) x[v][i] = __fadd_rn(x[v][i], r[i]);
+        }
         store_vec<DT, VW>(static_cast<T *>(a.rout) + row * a.ldro, col, x[v]);
       }
     } else {
@@ -73,11 +79,21 @@ __global__ void __launch_bounds__(row_max_threads(NV, VW)) add_rmsnorm_quant_ker
       for (int i = 0; i < VW; ++i) x[v][i] = 0.f;
     }
   }
+  // Squares two at a time; their sum stays in column order (the bits depend on it).
   float ss = 0.f;
 #pragma unroll
-  for (int v = 0; v < NV; ++v)
+  for (int v = 0; v < NV; ++v) {
+    float sq[VW];
+    if constexpr (VW % 2 == 0) {
 #pragma unroll
-    for (int i = 0; i < VW; ++i) ss = __fadd_rn(ss, __fmul_rn(x[v][i], x[v][i]));
+      for (int i = 0; i < VW; i += 2) mul2_rn(sq[i], sq[i + 1], x[v][i], x[v][i + 1], x[v][i], x[v][i + 1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) sq[i] = __fmul_rn(x[v][i], x[v][i]);
+    }
+#pragma unroll
+    for (int i = 0; i < VW; ++i) ss = __fadd_rn(ss, sq[i]);
+  }
   ss = block_sum(ss, red);
   // var = sum(x^2) / K with Triton's plain `/`, then xn = x * rsqrt(var + eps).
   const float var = div_full(ss, static_cast<float>(a.K));
@@ -85,9 +101,20 @@ __global__ void __launch_bounds__(row_max_threads(NV, VW)) add_rmsnorm_quant_ker
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
     const int col = col_of<VW>(v);
+    if (col >= a.K) continue;
+    if constexpr (VW % 2 == 0 && WDT >= 0) {
+      // y = round(round_w(x * rs) * w), two columns per instruction
 #pragma unroll
-    for (int i = 0; i < VW; ++i) {
-      if (col < a.K) {
+      for (int i = 0; i < VW; i += 2) {
+        float n0, n1;
+        mul2_rn(n0, n1, x[v][i], x[v][i + 1], rs, rs);
+        round2_through<WDT>(n0, n1);
+        mul2_rn(x[v][i], x[v][i + 1], n0, n1, wv[v][i], wv[v][i + 1]);
+        round2_through<DT>(x[v][i], x[v][i + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) {
         const float xn = round_to_weight(__fmul_rn(x[v][i], rs), wdt);
         x[v][i] = round_through<DT>(__fmul_rn(xn, wv[v][i]));
       }

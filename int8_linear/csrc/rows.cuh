@@ -140,16 +140,35 @@ __device__ __forceinline__ void quantize_vals(const float (&y)[NV][VW], int K, i
   for (int v = 0; v < NV; ++v) {
     const int col = col_of<VW>(v);
     if (col >= K) continue;
-    int8_t q[VW];
+    float p[VW];
+    if constexpr (VW % 2 == 0) {
 #pragma unroll
-    for (int i = 0; i < VW; ++i) {
-      int r = __float2int_rn(__fmul_rn(y[v][i], inv));
-      r = r < -128 ? -128 : (r > 127 ? 127 : r);
-      q[i] = static_cast<int8_t>(r);
+      for (int i = 0; i < VW; i += 2) mul2_rn(p[i], p[i + 1], y[v][i], y[v][i + 1], inv, inv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VW; ++i) p[i] = __fmul_rn(y[v][i], inv);
     }
     if constexpr (VW == 8) {
-      *reinterpret_cast<uint2 *>(qrow + col) = *reinterpret_cast<const uint2 *>(q);
+      // cvt.pack.sat: two int32 saturated to [-128, 127] and packed per instruction
+      // (the clamp and the byte packing in one step).
+      uint32_t w[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r0 = __float2int_rn(p[4 * h]), r1 = __float2int_rn(p[4 * h + 1]);
+        const int r2 = __float2int_rn(p[4 * h + 2]), r3 = __float2int_rn(p[4 * h + 3]);
+        uint32_t t;
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(t) : "r"(r3), "r"(r2));
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w[h]) : "r"(r1), "r"(r0), "r"(t));
+      }
+      *reinterpret_cast<uint2 *>(qrow + col) = make_uint2(w[0], w[1]);
     } else {
+      int8_t q[VW];
+#pragma unroll
+      for (int i = 0; i < VW; ++i) {
+        int r = __float2int_rn(p[i]);
+        r = r < -128 ? -128 : (r > 127 ? 127 : r);
+        q[i] = static_cast<int8_t>(r);
+      }
 #pragma unroll
       for (int i = 0; i < VW; ++i) qrow[col + i] = q[i];
     }
