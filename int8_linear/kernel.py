@@ -234,6 +234,7 @@ def w8a8_mm(
     config: Config | None = None,
     raw: bool = False,
     cached_launch: bool = True,
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """(A_q @ B_q) * scale_a * scale_b + bias, for int8 A_q [M, K] and B_q [K, N].
 
@@ -241,7 +242,9 @@ def w8a8_mm(
     [N, 1]) or a scalar, both float32.  With raw=True the exact int32 product is
     returned and the scales and bias are ignored.  Raises NotSupported for what the
     kernel does not take (the caller may fall back) and ValueError for inconsistent
-    arguments, as the reference does (int8_linear/kernel.py:221-240).
+    arguments, as the reference does (int8_linear/kernel.py:221-240).  `out` (an
+    addition to the reference's signature) is an [M, N] tensor of the output dtype
+    with contiguous rows to write into instead of a new one.
     """
     del cached_launch  # launches never go through a JIT dispatch here
     if a_q.dtype != torch.int8 or b_q.dtype != torch.int8:
@@ -273,7 +276,13 @@ def w8a8_mm(
         raise ValueError("w8a8_mm runs on a CUDA device; got tensors on "
                          f"{a_q.device}, {b_q.device}, {sa.device}, {sb.device}")
 
-    out = torch.empty((m, n), dtype=torch.int32 if raw else out_dtype, device=a_q.device)
+    want_dtype = torch.int32 if raw else out_dtype
+    if out is None:
+        out = torch.empty((m, n), dtype=want_dtype, device=a_q.device)
+    elif tuple(out.shape) != (m, n) or out.dtype != want_dtype or out.device != a_q.device \
+            or (n > 1 and out.stride(1) != 1):
+        raise ValueError(f"out must be a {want_dtype} [{m}, {n}] tensor with contiguous rows on "
+                         f"{a_q.device}, got {out.dtype} {tuple(out.shape)} strides {out.stride()}")
     if m == 0 or n == 0:
         return out
     a = _aligned_rows(a_q)

@@ -315,3 +315,25 @@ def test_dequant_i32_equals_the_gemm_epilogue(dtype, m, k, n):
     acc = w8a8_mm(a, w.t(), one(), one(), raw=True)
     got = dequant_i32(acc, sa, sb, dtype, bias)
     assert torch.equal(got, w8a8_mm(a, w.t(), sa, sb, dtype, bias))
+
+
+def test_out_argument_writes_in_place_with_the_same_bits():
+    """`out=`: the product written into a given tensor (a slice of a larger buffer
+    here) equals the returned one; a tensor of the wrong shape or dtype is refused."""
+    m, k, n = 5, 2048, 1024
+    a, w = ints((m, k), 400), ints((n, k), 401)
+    g = torch.Generator().manual_seed(402)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3).cuda()
+    want = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16)
+    buf = torch.full((3 * m * n,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    out = buf[m * n: 2 * m * n].view(m, n)
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, out=out)
+    assert got.data_ptr() == out.data_ptr()
+    assert np.array_equal(bits(out), bits(want))
+    assert torch.isnan(buf[:m * n].float()).all() and torch.isnan(buf[2 * m * n:].float()).all()
+    raw = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    w8a8_mm(a, w.t(), sa, sb, raw=True, out=raw)
+    assert np.array_equal(np_(raw), exact(a, w))
+    with pytest.raises(ValueError, match="out must be"):
+        w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, out=torch.empty((m, n), device="cuda"))
