@@ -153,12 +153,27 @@ __global__ void __launch_bounds__(row_max_threads(NV, VW)) silu_mul_quant_kernel
       float g[VW], u[VW];
       load_vec<DT, VW>(grow, col, g);
       load_vec<DT, VW>(urow, col, u);
+      if constexpr (VW % 2 == 0) {
+        // silu(g) = g / (1 + exp(-g)) with Triton's plain `/`; the sums, products and
+        // roundings two columns per instruction.
 #pragma unroll
-      for (int i = 0; i < VW; ++i) {
-        // silu(g) = g / (1 + exp(-g)) with Triton's plain `/`.
-        float s = div_full(g[i], __fadd_rn(1.0f, expf(-g[i])));
-        if (a.round_silu) s = round_through<DT>(s);
-        y[v][i] = round_through<DT>(__fmul_rn(s, u[i]));
+        for (int i = 0; i < VW; i += 2) {
+          float d0, d1, s0, s1;
+          add2_rn(d0, d1, 1.0f, 1.0f, expf(-g[i]), expf(-g[i + 1]));
+          s0 = div_full(g[i], d0);
+          s1 = div_full(g[i + 1], d1);
+          if (a.round_silu) round2_through<DT>(s0, s1);
+          mul2_rn(y[v][i], y[v][i + 1], s0, s1, u[i], u[i + 1]);
+          round2_through<DT>(y[v][i], y[v][i + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < VW; ++i) {
+          // silu(g) = g / (1 + exp(-g)) with Triton's plain `/`.
+          float s = div_full(g[i], __fadd_rn(1.0f, expf(-g[i])));
+          if (a.round_silu) s = round_through<DT>(s);
+          y[v][i] = round_through<DT>(__fmul_rn(s, u[i]));
+        }
       }
     } else {
 #pragma unroll
