@@ -108,7 +108,10 @@ def alg_bytes(m, k, n, bias) -> int:
 
 # ------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region.
+    Entering waits (up to 3 s) for nvidia-smi's first sample, so sampling runs before the
+    region starts; leaving waits (up to 1 s) for a sample taken after the region began, so
+    a region shorter than the 50 ms interval still has one."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -118,6 +121,7 @@ class ClockSampler:
         self.dev = device_index
         self.proc = None
         self.lines: list[str] = []
+        self.start = 0
 
     def __enter__(self):
         try:
@@ -127,6 +131,10 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.start = len(self.lines)
         except OSError:
             self.proc = None
         return self
@@ -137,6 +145,9 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            t0 = time.time()
+            while len(self.lines) <= self.start and time.time() - t0 < 1.0 and self.proc.poll() is None:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -146,7 +157,7 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.start:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 8:
                 continue

@@ -1,45 +1,47 @@
-"""Tensor parallelism on 2 GPUs: the TP stand-in decoder (NCCL collectives or this
-library's NVLink exchange kernels) and each exchange kernel give exactly the one-GPU
-results.  Needs two GPUs; skipped otherwise."""
+"""Tensor parallelism: the TP stand-in decoder (NCCL collectives or this library's NVLink
+exchange kernels) and each exchange kernel give exactly the one-GPU results.  Runs on 2
+GPUs (I8L_TP_WORLD=4 or 8 for more); skipped when the box has fewer."""
 
 from __future__ import annotations
 
 import datetime
 import os
-import socket
+import tempfile
 
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-WORLD = 2
+WORLD = int(os.environ.get("I8L_TP_WORLD", "2"))
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous_file():
+    """A fresh file for the process group's rendezvous (no TCP port to race for)."""
+    fd, path = tempfile.mkstemp(prefix="i8l_tp_")
+    os.close(fd)
+    os.unlink(path)
+    return path
 
 
-def _init(rank, port):
+def _init(rank, path):
     import torch.distributed as dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=WORLD, device_id=dev,
-                            timeout=datetime.timedelta(seconds=120))
+    dist.init_process_group("nccl", init_method=f"file://{path}", rank=rank, world_size=WORLD,
+                            device_id=dev, timeout=datetime.timedelta(seconds=120))
     return dev
 
 
-def _worker(rank, port, m, mode, q):
+def _worker(rank, path, m, mode, q):
     import torch.distributed as dist
 
     from int8_linear import set_pdl
     from int8_linear.standin import StandinDecoder, TPStandinDecoder
     from int8_linear.tp import PeerComm
 
-    dev = _init(rank, port)
+    dev = _init(rank, path)
     comm = None
     try:
         set_pdl(True)
@@ -67,8 +69,8 @@ def _run(target, *args):
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=target, args=(r, port, *args, q)) for r in range(WORLD)]
+    path = _rendezvous_file()
+    procs = [ctx.Process(target=target, args=(r, path, *args, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(WORLD)]
@@ -78,7 +80,7 @@ def _run(target, *args):
     return res
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason=f"needs {WORLD} GPUs")
 @pytest.mark.parametrize("mode", ["nccl", "peer"])
 @pytest.mark.parametrize("m", [1, 16])
 def test_tp_standin_equals_one_gpu(m, mode):
@@ -87,14 +89,14 @@ def test_tp_standin_equals_one_gpu(m, mode):
         assert same, f"rank {rank}: TP output differs from the one-GPU stand-in"
 
 
-def _ops_worker(rank, port, q):
+def _ops_worker(rank, path, q):
     import torch.distributed as dist
 
     from int8_linear import fused_quant as fq
     from int8_linear import tp
     from int8_linear.kernel import w8a8_mm
 
-    dev = _init(rank, port)
+    dev = _init(rank, path)
     comm = None
     fails = []
     try:
@@ -147,7 +149,7 @@ def _ops_worker(rank, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason=f"needs {WORLD} GPUs")
 def test_peer_exchange_ops_equal_one_gpu():
     """Every exchange kernel on two GPUs gives what one GPU gives on the whole row."""
     for rank, fails, status in _run(_ops_worker):
