@@ -190,3 +190,21 @@ def test_decode_batch_rows_equal_large_batch_rows(kind, m, cols, dtype):
         q2, s2 = fq.per_token_quant(xs)
         qo, so = oq.quant_ieee(np_(xs))
         check(q2, s2, qo, so, exact=True)
+
+
+@pytest.mark.parametrize("m,k", [(2049, 2048), (4096, 2048), (2049, 4096), (2048, 8192), (2048, 1000)])
+@pytest.mark.parametrize("act,wdt", [(torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32)])
+def test_large_batch_norm_rows_equal_small_batch_rows(m, k, act, wdt):
+    """Large batches normalise two rows per CTA (odd batches end with a one-row CTA); each
+    row's arithmetic is the one-row kernel's, so rows agree bit for bit with the same rows
+    in a small batch, residual output included."""
+    x, r = rand((m, k), 500 + m, dtype=act), rand((m, k), 501 + m, dtype=act)
+    w = (rand((k,), 502, 0.1, torch.float32) + 1.0).to(wdt)
+    q0, s0, r0 = fq.add_rmsnorm_quant(x, r, w, EPS)
+    for lo, hi in ((0, 5), (m - 3, m)):
+        q1, s1, r1 = fq.add_rmsnorm_quant(x[lo:hi].contiguous(), r[lo:hi].contiguous(), w, EPS)
+        assert torch.equal(q1, q0[lo:hi]) and torch.equal(s1, s0[lo:hi]), (lo, hi)
+        assert np.array_equal(bits(r1), bits(r0[lo:hi]))
+    q2, s2, _ = fq.add_rmsnorm_quant(x, None, w, EPS)
+    q3, s3, _ = fq.add_rmsnorm_quant(x[-3:].contiguous(), None, w, EPS)
+    assert torch.equal(q3, q2[-3:]) and torch.equal(s3, s2[-3:])
