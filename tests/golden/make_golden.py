@@ -1,6 +1,6 @@
 """Writes tests/golden/golden.npz and golden.json from the REFERENCE's own functions.
 
-    python tests/golden/make_golden.py [--reference /path/to/int8-linear]
+    python tests/golden/make_golden.py --reference /path/to/int8-linear
 
 Runs on a CPU in the build container, where the reference package is importable
 (its Triton kernels are never run; only its torch reference functions are):
@@ -46,7 +46,8 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the reference repository (AshrithaG/int8-linear)")
     a = ap.parse_args()
     ref_root = Path(a.reference)
     sys.path.insert(0, str(ref_root))   # the reference package shadows nothing here
