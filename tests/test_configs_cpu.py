@@ -40,3 +40,24 @@ def test_tuned_table_entries_are_valid_tilings():
                 assert entry.get("graph_us", entry.get("stand_in_us", 0)) > 0
                 count += 1
     assert count > 0
+
+
+def test_tuner_weight_pools_cover_twice_the_l2():
+    from int8_linear.tune import COPIES, L2_BYTES, pool_size
+
+    for nbytes in (4096 * 2048, 2048 * 2048, 12288 * 2048, 28672 * 4096, 1 << 30):
+        n = pool_size(nbytes)
+        assert n >= COPIES and n * nbytes >= 2 * L2_BYTES, nbytes
+
+
+@pytest.mark.parametrize("m", [1, 2, 4, 16, 17, 64, 256, 1024, 4096])
+@pytest.mark.parametrize("k,n", [(2048, 4096), (6144, 2048), (4096, 28672)])
+def test_tuner_candidates_are_valid_and_narrow_only_for_small_batches(m, k, n):
+    from int8_linear.tune import candidates
+
+    cands = candidates(m, n, k, 148)
+    assert cands and len({c.name for c in cands}) == len(cands)
+    for c in cands:
+        c.check()
+        if c.split == 3 and not c.swapped:
+            assert m <= 16, c.name
