@@ -9,7 +9,7 @@ equal the one-process result bit for bit, as it does on GPUs with the CUDA kerne
 from __future__ import annotations
 
 import os
-import socket
+import tempfile
 
 import numpy as np
 import pytest
@@ -73,11 +73,10 @@ def problem():
     return a_q, a_s, w, w_s, bias, x, gu
 
 
-def _worker(rank, port, q):
+def _worker(rank, path, q):
     from int8_linear import tp
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    dist.init_process_group("gloo", init_method=f"file://{path}", rank=rank, world_size=WORLD)
     try:
         ops = OracleOps()
         a_q, a_s, w, w_s, bias, x, gu = problem()
@@ -101,18 +100,20 @@ def _worker(rank, port, q):
         dist.destroy_process_group()
 
 
-def free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def rendezvous_file():
+    """A fresh file for the process group's rendezvous (no TCP port to race for)."""
+    fd, path = tempfile.mkstemp(prefix="i8l_gloo_")
+    os.close(fd)
+    os.unlink(path)
+    return path
 
 
 @pytest.fixture(scope="module")
 def results():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    path = rendezvous_file()
+    procs = [ctx.Process(target=_worker, args=(r, path, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     out = {}
