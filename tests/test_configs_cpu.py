@@ -61,3 +61,25 @@ def test_tuner_candidates_are_valid_and_narrow_only_for_small_batches(m, k, n):
         c.check()
         if c.split == 3 and not c.swapped:
             assert m <= 16, c.name
+
+
+def test_fused_activation_tiling_is_the_swap_tile_with_direct_loads():
+    from int8_linear.kernel import fused_act_config
+
+    assert fused_act_config(Config(16, 128, split=3, cluster=4)) == Config(16, 128, split=3, cluster=4, act=2)
+    assert fused_act_config(Config(32, 128, act=2)) == Config(32, 128, act=2)
+    assert fused_act_config(Config(128, 256, split=3, cluster=8)) is None   # narrow: no direct loads
+    assert fused_act_config(Config(128, 256)) is None
+
+
+def test_fused_activation_entry_validates_before_touching_a_gpu():
+    import torch
+
+    from int8_linear import NotSupported, w8a8_mm_quant_act
+
+    w = torch.zeros((64, 32), dtype=torch.int8)
+    sb = torch.ones(1)
+    with pytest.raises(NotSupported, match="bf16/fp16"):
+        w8a8_mm_quant_act(torch.zeros((2, 64)), w, sb)                     # fp32 activation
+    with pytest.raises(ValueError, match="cannot multiply"):
+        w8a8_mm_quant_act(torch.zeros((2, 48), dtype=torch.bfloat16), w, sb)
