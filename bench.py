@@ -8,11 +8,13 @@ Workload: the per-layer sweep at the Qwen3-1.7B shapes vLLM 
 {1,2,4,8,16,17,32,64,128,256,1024,4096}, with and without a bf16 bias.  Inputs are
 generated as in config 0 (bf16 N(0,1) activations and N(0,0.02) weights, quantised per
 row to int8).  One step runs every (layer, M, bias) GEMM R=8 times back to back from a
-CUDA graph, each launch on its own weight copy, so weights are always L2-cold (8 copies
-of every layer, 400 MB, far above the 126 MB L2).  `value` is microseconds per sweep:
-one GEMM of every (layer, M, bias), device time.  `e2e` is the same sweep through the
-public API w8a8_mm, eagerly, with each step's int8 activations and scales copied in
-from pinned host memory and every output copied back.
+CUDA graph, each launch on its own weight copy taken from a per-layer pool of copies
+that together hold at least twice the 126 MB L2 (each case on the next window of 8), so
+weights are always L2-cold; the per-case timings also flush L2 before every timed
+replay.  `value` is microseconds per sweep: one GEMM of every (layer, M, bias), device
+time.  `e2e` is the same sweep through the public API w8a8_mm, eagerly, with each step's
+int8 activations and scales copied in from pinned host memory and every output copied
+back (packed per group of cases, the two directions overlapped on their own streams).
 
 Under torchrun (N > 1) each rank runs its column shard (N/g output columns) of every
 layer, independently; the NCCL all-gather of the shards is timed separately and
