@@ -1,28 +1,36 @@
-"""Benchmark of the W8A8 hot path on B200, one JSON line on rank 0.
+"""Benchmark of the W8A8 hot path on B200; rank 0 prints one short JSON line last.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--model qwen3-1.7b-vllm|llama-3-8b] [--no-standin]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-triton]
+                    [--model qwen3-1.7b-vllm|llama-3-8b] [--no-standin] [--no-e2e] [--no-pdl]
+                    [--out FILE] [--detail FILE]
+    python bench.py --case gemm|sweep|quant|standin [--shape ...] [...]   (profiling workloads)
 
 Workload: the per-layer sweep at the Qwen3-1.7B shapes vLLM runs
 (qkv 2048x4096, o_proj 2048x2048, gate_up 2048x12288, down 6144x2048), every M in
-{1,2,4,8,16,17,32,64,128,256,1024,4096}, with and without a bf16 bias.  Inputs are
-generated as in config 0 (bf16 N(0,1) activations and N(0,0.02) weights, quantised per
-row to int8).  One step runs every (layer, M, bias) GEMM R=8 times back to back from a
-CUDA graph, each launch on its own weight copy taken from a per-layer pool of copies
-that together hold at least twice the 126 MB L2 (each case on the next window of 8), so
-weights are always L2-cold; the per-case timings also flush L2 before every timed
-replay.  `value` is microseconds per sweep: one GEMM of every (layer, M, bias), device
-time.  `e2e` is the same sweep through the public API w8a8_mm, eagerly, with each step's
-int8 activations and scales copied in from pinned host memory and every output copied
-back (packed per group of cases, the two directions overlapped on their own streams).
+{1,2,4,8,16,17,32,64,128,256,1024,4096}, with and without a bf16 bias: 96 GEMMs.
+Inputs are generated as in config 0 (bf16 N(0,1) activations and N(0,0.02) weights,
+quantised per row to int8).  Before anything is timed every case runs once into an
+output filled with NaN and is checked against the reference's float64 layer and,
+bit for bit, against the fp32 epilogue order (`checked` in the line).  One step runs
+every case R=8 times back to back from CUDA graphs, each launch on its own weight copy
+from a per-layer pool holding at least twice the 126 MB L2, so weights are always
+L2-cold.  `value` is microseconds per sweep (one GEMM of each case), device time.
+`e2e` is the same sweep through the public API w8a8_mm, eagerly, with each step's int8
+activations and scales copied in from pinned host memory and every output copied back.
+
+The final line keeps to a few KB (the driver reads the tail of stdout); the per-shape
+table, the L2-warm timings and the full quantiser table go to --detail (default
+gpurun_out/bench_detail_n<N>.json).
 
 Under torchrun (N > 1) each rank runs its column shard (N/g output columns) of every
 layer, independently; the NCCL all-gather of the shards is timed separately and
-reported as `allgather_us_per_sweep`.
+reported as `allgather_us_per_sweep`.  The config-2 (Llama-3-8B) sweep is run the same
+way and reported as `config2_us_per_sweep`, and the stand-in decoder runs tensor
+parallel in both exchange modes.
 
---impl reference times the reference's CPU implementation of the path (the float64
-torch layer of bench/bench_linear.py:164-165, restated in oracle/gemm.py) on this
-host's cores, on a bounded sample of the same sweep, on rank 0 only.
+--impl reference times the reference's CPU implementation of the path on this host's
+cores: the float64 torch layer of bench/bench_linear.py:164-165 (restated in
+oracle/gemm.py layer_f64_torch) over the whole sweep, every M and N, on rank 0 only.
 """
 
 from __future__ import annotations
@@ -44,9 +52,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "W8A8 GEMM µs & roofline % per (M,K,N); stand-in decode µs/layer at bs 1–128"
 M_SWEEP = [1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 1024, 4096]
 QUANT_M = [1, 16, 64, 128, 1024, 4096]    # BASELINE config 3 batch sizes timed
+QUANT_M_LINE = ["1", "128", "4096"]       # the ones the final line carries
 STANDIN_BATCHES = [1, 2, 4, 8, 16, 32, 64, 128]
 COPIES = 8          # launches per shape per step, each on its own weight copy
 L2_BYTES = 126 << 20
+LINE_LIMIT = 4000   # bytes of the final JSON line
 
 
 def pool_size(nbytes: int) -> int:
@@ -72,26 +82,36 @@ def flush_l2():
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=60)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference", "reference-triton", "reference-triton-child"],
                     default="ours")
     ap.add_argument("--model", default="qwen3-1.7b-vllm")
     ap.add_argument("--no-standin", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
-    ap.add_argument("--out", default=None, help="also write the JSON line to this file")
+    ap.add_argument("--no-config2", action="store_true", help="skip the config-2 (Llama-3-8B) sweep")
+    ap.add_argument("--out", default=None, help="also write the final JSON line to this file")
+    ap.add_argument("--detail", default=None, help="where the per-shape tables go")
+    # profiling workloads (small, self-contained; for ncu captures)
+    ap.add_argument("--case", choices=["gemm", "sweep", "quant", "standin"], default=None)
+    ap.add_argument("--shape", default=None, help="gemm: M,N,K; quant: M; standin: batch")
+    ap.add_argument("--config", default=None, help="gemm: bm,bn[,split[,cluster]]")
+    ap.add_argument("--kind", default="norm", choices=["norm", "silu", "plain"])
+    ap.add_argument("--iters", type=int, default=4)
     return ap.parse_args()
 
 
-def peaks() -> dict:
+def peaks(int8_tops: float | None = None) -> dict:
     p = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
         d = json.loads(f.read_text())
         p = {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
-    # Dense int8 tensor throughput is twice dense bf16 on B200 (4.5 vs 2.25 POPS).
-    p["int8_tops"] = 2.0 * p["bf16_tflops"]
+    if int8_tops:
+        p["int8_tops"], p["int8_source"] = int8_tops, "measured int8 on this box (int8_tops_measured)"
+    else:
+        p["int8_tops"], p["int8_source"] = 2.0 * p["bf16_tflops"], p["source"] + " bf16 x2"
     return p
 
 
@@ -106,6 +126,16 @@ def layers_for(model: str):
 def alg_bytes(m, k, n, bias) -> int:
     """Bytes the GEMM must move at least once: A, W, scales, bias, bf16 output."""
     return m * k + n * k + 4 * m + 4 * n + (2 * n if bias else 0) + 2 * m * n
+
+
+def cpu_model() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 # ------------------------------------------------------------------- clocks
@@ -255,71 +285,237 @@ def time_graph(graph, windows=5, flush=True):
     return statistics.median(ts)
 
 
-# ------------------------------------------------------------------- our arm
-def run_ours(args, world, rank, dev):
+def launcher(acts, lay, m, bias, copies):
+    """The graphed body of one case: w8a8_mm of the case's activation on each weight copy."""
     import torch
-    import torch.distributed as dist
 
     from int8_linear import w8a8_mm
-    from int8_linear.kernel import choose_config
 
-    pk = peaks()
-    layers, acts = build_operands(args.model, world, rank, dev)
-    cases = sweep_cases(layers)
+    a_q, a_s = acts[(m, lay["k"])]
+    b = lay["bias"] if bias else None
 
-    def launcher(lay, m, bias, copies):
-        a_q, a_s = acts[(m, lay["k"])]
-        b = lay["bias"] if bias else None
+    def fn():
+        for wq, ws in copies:
+            w8a8_mm(a_q, wq.t(), a_s, ws, torch.bfloat16, b)
+    return fn
 
-        def fn():
-            for wq, ws in copies:
-                w8a8_mm(a_q, wq.t(), a_s, ws, torch.bfloat16, b)
-        return fn
 
-    # per-shape graphs: COPIES launches on distinct weight copies, each case on the next
-    # window of its layer's pool (L2-cold in the timed region too, where the cases of a
-    # layer run back to back)
-    graphs, per_shape, window = [], [], {}
+def capture_sweep(layers, acts, cases):
+    """Per-case graphs: COPIES launches on distinct weight copies, each case on the next
+    window of its layer's pool (L2-cold in the timed region too, where the cases of a
+    layer run back to back)."""
+    graphs, window = [], {}
     for lay, m, bias in cases:
         w0 = window.get(lay["name"], 0)
         window[lay["name"]] = (w0 + COPIES) % len(lay["copies"])
-        g = capture(launcher(lay, m, bias, lay["copies"][w0:w0 + COPIES]))
-        graphs.append(g)
+        graphs.append(capture(launcher(acts, lay, m, bias, lay["copies"][w0:w0 + COPIES])))
+    return graphs
+
+
+# ------------------------------------------------------------------- output checks
+def check_case(a_q, a_s, wq, ws, bias) -> tuple[bool, float]:
+    """Runs w8a8_mm once into an output filled with NaN and compares it with (1) the fp32
+    epilogue order of the reference kernel (int8_linear/kernel.py:109-120: f32(acc)*sa,
+    *sb, +bias, one rounding), bit for bit, and (2) the reference's float64 layer
+    (bench/bench_linear.py:164-165), by the relative error its check uses
+    (bench_linear.py:185-192).  The int32 product is a float64 GEMM of int8 values, exact
+    in any order.  Returns (bit-exact, max relative error)."""
+    import torch
+
+    from int8_linear import w8a8_mm
+
+    m, n = a_q.shape[0], wq.shape[0]
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=a_q.device)
+    w8a8_mm(a_q, wq.t(), a_s, ws, torch.bfloat16, bias, out=out)
+    acc64 = a_q.double() @ wq.double().t()
+    v = acc64.to(torch.int32).to(torch.float32) * a_s.reshape(-1, 1)
+    v = v * ws.reshape(1, -1)
+    if bias is not None:
+        v = v + bias.float().reshape(1, -1)
+    exact = torch.equal(out.view(torch.int16), v.to(torch.bfloat16).view(torch.int16))
+    term = acc64 * a_s.double().reshape(-1, 1) * ws.double().reshape(1, -1)
+    ref = term + bias.double().reshape(1, -1) if bias is not None else term
+    scale = torch.maximum(ref.abs(), term.abs()).clamp_min(1e-6)
+    rel = ((out.double() - ref).abs() / scale).max().item()
+    return exact, rel
+
+
+def check_sweep(layers, acts, cases) -> dict:
+    import torch
+
+    ok = exact = 0
+    worst = 0.0
+    for lay, m, bias in cases:
+        a_q, a_s = acts[(m, lay["k"])]
+        wq, ws = lay["copies"][0]
+        e, rel = check_case(a_q, a_s, wq, ws, lay["bias"] if bias else None)
+        exact += int(e)
+        ok += int(e and rel <= 1e-2)
+        worst = max(worst, rel)
+    torch.cuda.synchronize()
+    return {"checked": f"{ok}/{len(cases)}", "bit_exact": exact, "max_rel_err_f64": float(f"{worst:.3g}")}
+
+
+# ------------------------------------------------------------------- int8 peak
+def int8_peak_probe(dev) -> dict:
+    """Dense int8 throughput at 8192^3, best of 10 (CUDA events): torch._int_mm (cuBLASLt)
+    and this library's w8a8_mm (int32 out, the library's tile).  The larger is the tensor
+    roofline's peak."""
+    import torch
+
+    from int8_linear import w8a8_mm
+
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(7)
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=g)
+    sa = torch.ones((n, 1), device=dev)
+    out = {}
+
+    def best(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e-3)
+        return round(2.0 * n ** 3 / min(ts) / 1e12, 1)
+
+    try:
+        out["torch_int_mm"] = best(lambda: torch._int_mm(a, b.t()))
+    except RuntimeError as e:  # noqa: BLE001
+        out["torch_int_mm"] = None
+        out["torch_int_mm_error"] = str(e).splitlines()[0][:120]
+    o32 = torch.empty((n, n), dtype=torch.int32, device=dev)
+    out["ours_i32"] = best(lambda: w8a8_mm(a, b.t(), sa, sa, raw=True, out=o32))
+    out["peak"] = max(v for v in (out.get("torch_int_mm"), out["ours_i32"]) if v)
+    del a, b, o32
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------- tie counts
+def tie_counts(dev) -> dict:
+    """BASELINE config 3 at M=4096: our fused quantisers against the reference's torch
+    references (tests/test_fused_quant.py:26-51, restated here in torch on the GPU as the
+    reference's test runs them): how many int8 values differ (each by one step, at a
+    rounding tie or a boundary that a different summation order moves), and the largest
+    difference."""
+    import torch
+
+    from int8_linear import fused_quant as fq
+
+    g = torch.Generator(device=dev).manual_seed(3)
+    m, k, i = 4096, 2048, 6144
+    x = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+    r = torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn(k, generator=g, device=dev)).to(torch.bfloat16)
+    gu = torch.randn((m, 2 * i), generator=g, device=dev).to(torch.bfloat16)
+
+    def quant(y):
+        yf = y.float()
+        absmax = yf.abs().amax(-1, keepdim=True)
+        inv = torch.where(absmax == 0, torch.zeros_like(absmax), 127.0 / absmax)
+        return torch.round(yf * inv).clamp(-128, 127).to(torch.int8), absmax / 127.0
+
+    xf = x.float() + r.float()
+    y = ((xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(w.dtype) * w).to(x.dtype)
+    q0, s0 = quant(y)
+    q, s, _ = fq.add_rmsnorm_quant(x, r, w, 1e-6, True)
+    gf, uf = gu[:, :i].float(), gu[:, i:].float()
+    a = (gf / (1.0 + torch.exp(-gf))).to(gu.dtype).float()
+    q1, s1 = quant((a * uf).to(gu.dtype))
+    qs, ss = fq.silu_mul_quant(gu, True, True)
+    out = {}
+    for name, got, want, sg, sw in (("add_rmsnorm_quant", q, q0, s, s0), ("silu_mul_quant", qs, q1, ss, s1)):
+        d = (got.int() - want.int()).abs()
+        out[name] = {"differ": int(d.ne(0).sum().item()), "numel": d.numel(),
+                     "max_abs": int(d.max().item()),
+                     "scale_rel": float(f"{((sg - sw).abs() / sw.clamp_min(1e-30)).max().item():.2g}")}
+    return out
+
+
+# ------------------------------------------------------------------- our arm
+def per_shape_timings(cases, graphs, pk):
+    from int8_linear.kernel import choose_config
+
+    rows = []
     for (lay, m, bias), g in zip(cases, graphs):
         us = time_graph(g) / COPIES
         k, n = lay["k"], lay["nl"]
         by, ops = alg_bytes(m, k, n, bias), 2 * m * n * k
         t_hbm, t_tc = by / (pk["hbm_gbs"] * 1e3), ops / (pk["int8_tops"] * 1e6)
-        per_shape.append({"layer": lay["name"], "M": m, "K": k, "N": n, "bias": bias, "us": round(us, 3),
-                          "bound": "hbm" if t_hbm >= t_tc else "tensor",
-                          "roof_frac": round(max(t_hbm, t_tc) / us, 4),
-                          "gbs": round(by / us / 1e3, 1), "tops": round(ops / us / 1e6, 1),
-                          "tile": choose_config(m, n, k).name})
-    # L2-warm numbers (the reference's method: the same weight replayed) for the no-bias sweep
-    warm = {}
-    for lay, m, bias in cases:
-        if bias:
-            continue
-        g = capture(launcher(lay, m, False, [lay["copies"][0]] * COPIES))
-        warm[f"{lay['name']}/{m}"] = round(time_graph(g, flush=False) / COPIES, 3)
-        del g
+        rows.append({"layer": lay["name"], "M": m, "K": k, "N": n, "bias": bias, "us": round(us, 3),
+                     "bound": "hbm" if t_hbm >= t_tc else "tensor",
+                     "roof_frac": round(max(t_hbm, t_tc) / us, 4),
+                     "gbs": round(by / us / 1e3, 1), "tops": round(ops / us / 1e6, 1),
+                     "tile": choose_config(m, n, k).name})
+    return rows
 
-    # ------------------------------------------------ timed region
+
+def roofline_of(per_shape, pk):
+    """Roofline of the GEMM kernel by class: Σ algorithmic bytes (HBM-bound decode
+    shapes) or ops (tensor-bound prefill shapes) over Σ CUDA-event time of the class.
+    `traffic` is ncu's DRAM bytes per launch of the class (profiles/gemm_traffic.json)."""
+    cls = {"hbm": [0.0, 0.0, 0], "tensor": [0.0, 0.0, 0]}
+    for row in per_shape:
+        k, n, m = row["K"], row["N"], row["M"]
+        amount = alg_bytes(m, k, n, row["bias"]) if row["bound"] == "hbm" else 2 * m * n * k
+        cls[row["bound"]][0] += amount
+        cls[row["bound"]][1] += row["us"]
+        cls[row["bound"]][2] += 1
+    tf = ROOT / "profiles" / "gemm_traffic.json"
+    traffic = json.loads(tf.read_text()) if tf.exists() else {}
+    total = cls["hbm"][1] + cls["tensor"][1]
+
+    def roof(kind):
+        amount, us, count = cls[kind]
+        if us == 0:
+            return None
+        if kind == "hbm":
+            ach = amount / us / 1e3
+            r = {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                 "frac": round(ach / pk["hbm_gbs"], 4), "traffic": traffic.get("hbm"),
+                 "peak_source": pk["source"] + " hbm copy"}
+        else:
+            ach = amount / us / 1e6
+            r = {"bound": "tensor", "achieved": round(ach, 1), "peak": pk["int8_tops"], "unit": "TOPS",
+                 "frac": round(ach / pk["int8_tops"], 4), "traffic": traffic.get("tensor"),
+                 "peak_source": pk["int8_source"]}
+        r["time_share"] = round(us / total, 3)
+        r["launches"] = count
+        return r
+
+    main = "hbm" if cls["hbm"][1] >= cls["tensor"][1] else "tensor"
+    return roof(main), roof("tensor" if main == "hbm" else "hbm")
+
+
+def timed_sweep(graphs, steps, warmup, world, dev, clocks=None):
+    """Device µs per step of replaying every graph once, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         for g in graphs:
             g.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    with ClockSampler(dev.index) as clocks:
+    ctx = clocks if clocks is not None else _Null()
+    with ctx:
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.nvtx.range_push("timed_region")   # `ncu --nvtx --nvtx-include timed_region/`
         t0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             for g in graphs:
                 g.replay()
         t1.record(stream)
@@ -327,45 +523,48 @@ def run_ours(args, world, rank, dev):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    ms = t0.elapsed_time(t1) / args.steps
+    ms = t0.elapsed_time(t1) / steps
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    return ms
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def run_ours(args, world, rank, dev):
+    import torch
+    import torch.distributed as dist
+
+    from int8_linear import w8a8_mm
+
+    peak = int8_peak_probe(dev) if world == 1 else None
+    pk = peaks(peak["peak"] if peak else None)
+    layers, acts = build_operands(args.model, world, rank, dev)
+    cases = sweep_cases(layers)
+    check = check_sweep(layers, acts, cases)
+    graphs = capture_sweep(layers, acts, cases)
+    per_shape = per_shape_timings(cases, graphs, pk)
+    # L2-warm numbers (the reference's method: the same weight replayed), no-bias cases
+    warm = {}
+    for lay, m, bias in cases:
+        if bias:
+            continue
+        g = capture(launcher(acts, lay, m, False, [lay["copies"][0]] * COPIES))
+        warm[f"{lay['name']}/{m}"] = round(time_graph(g, flush=False) / COPIES, 3)
+        del g
+
+    clocks = ClockSampler(dev.index)
+    ms = timed_sweep(graphs, args.steps, args.warmup, world, dev, clocks=clocks)
     value_us = ms * 1e3 / COPIES
-
-    # roofline of the GEMM kernel, by the class of launches that takes most of the time
-    cls = {"hbm": [0.0, 0.0], "tensor": [0.0, 0.0]}
-    for row in per_shape:
-        k, n, m = row["K"], row["N"], row["M"]
-        amount = alg_bytes(m, k, n, row["bias"]) if row["bound"] == "hbm" else 2 * m * n * k
-        cls[row["bound"]][0] += amount
-        cls[row["bound"]][1] += row["us"]
-    traffic = None
-    tf = ROOT / "profiles" / "gemm_traffic.json"
-    traffic_map = json.loads(tf.read_text()) if tf.exists() else {}
-
-    def roof(kind):
-        amount, us = cls[kind]
-        if us == 0:
-            return None
-        if kind == "hbm":
-            ach = amount / us / 1e3
-            return {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                    "frac": round(ach / pk["hbm_gbs"], 4), "traffic": traffic_map.get("hbm"),
-                    "time_share": None, "peak_source": pk["source"] + " hbm copy"}
-        ach = amount / us / 1e6
-        return {"bound": "tensor", "achieved": round(ach, 1), "peak": pk["int8_tops"], "unit": "TOPS",
-                "frac": round(ach / pk["int8_tops"], 4), "traffic": traffic_map.get("tensor"),
-                "time_share": None, "peak_source": pk["source"] + " bf16 x2 (dense int8 = 2x bf16)"}
-
-    total_us = cls["hbm"][1] + cls["tensor"][1]
-    main_kind = "hbm" if cls["hbm"][1] >= cls["tensor"][1] else "tensor"
-    roofline, other = roof(main_kind), roof("tensor" if main_kind == "hbm" else "hbm")
-    for r, kind in ((roofline, main_kind), (other, "tensor" if main_kind == "hbm" else "hbm")):
-        if r:
-            r["time_share"] = round(cls[kind][1] / total_us, 3)
-    del traffic
+    roofline, other = roofline_of(per_shape, pk)
 
     # ------------------------------------------------ all-gather of column shards
     allgather_us = None
@@ -394,12 +593,24 @@ def run_ours(args, world, rank, dev):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(layers, acts, cases, dev, world, max(1, min(args.steps, 5)))
+    del graphs, layers, acts
+    torch.cuda.empty_cache()
 
-    del graphs
-    standin = quant = standin_tp = standin_tp_peer = host = None
+    # ------------------------------------------------ config 2 (Llama-3-8B), same method
+    config2 = None
+    if not args.no_config2 and args.model != "llama-3-8b":
+        l2, a2 = build_operands("llama-3-8b", world, rank, dev)
+        c2 = sweep_cases(l2)
+        g2 = capture_sweep(l2, a2, c2)
+        config2 = round(timed_sweep(g2, 3, 2, world, dev) * 1e3 / COPIES, 2)
+        del g2, l2, a2, c2
+        torch.cuda.empty_cache()
+
+    standin = quant = standin_tp = standin_tp_peer = host = ties = None
     if not args.no_standin and world == 1:
         standin = run_standin(dev)
-        quant = run_quantisers(dev)
+        quant = run_quantisers(dev, pk)
+        ties = tie_counts(dev)
         import int8_linear.vllm_patch  # noqa: F401  (registers the custom op)
         from int8_linear import fused_quant as fq_ours
         host = host_cost(w8a8_mm, torch.ops.int8_linear.w8a8_mm, fq_ours, dev)
@@ -414,14 +625,20 @@ def run_ours(args, world, rank, dev):
             comm.close()
 
     launches = args.steps * len(cases) * COPIES
-    return {
-        "value": round(value_us, 2), "ms_per_step": round(ms, 4), "per_shape": per_shape,
-        "l2_warm_us": warm, "roofline": roofline, "roofline_other": other,
-        "allgather_us_per_sweep": allgather_us, "e2e": e2e, "standin_us_per_layer": standin,
-        "quantisers": quant, "standin_tp_us_per_layer": standin_tp,
-        "standin_tp_peer_us_per_layer": standin_tp_peer, "host_us_per_call": host,
-        "clocks": clocks.summary(), "gpu_launches": launches,
+    line = {
+        "value": round(value_us, 2), "ms_per_step": round(ms, 4), "roofline": roofline,
+        "roofline_other": other, "int8_tops_measured": peak, **check, "e2e": e2e,
+        "allgather_us_per_sweep": allgather_us, "config2_us_per_sweep": config2,
+        "standin_us_per_layer": standin,
+        "quantisers_us": ({m: [quant[m]["add_rmsnorm_quant_us"], quant[m]["silu_mul_quant_us"]]
+                           for m in QUANT_M_LINE} if quant else None),
+        "ties_4096": ({k: v["differ"] for k, v in ties.items()} if ties else None),
+        "standin_tp_us_per_layer": standin_tp, "standin_tp_peer_us_per_layer": standin_tp_peer,
+        "host_us_per_call": host, "clocks": clocks.summary(), "gpu_launches": launches,
     }
+    detail = {"per_shape": per_shape, "l2_warm_us": warm, "quantisers": quant, "ties": ties,
+              "int8_tops_measured": peak}
+    return line, detail
 
 
 def host_cost(mm, op, fq, dev) -> dict:
@@ -429,8 +646,6 @@ def host_cost(mm, op, fq, dev) -> dict:
     at M=1 (qkv 2048 x 4096), where the host, not the GPU, sets the pace.  The same
     function times both arms (`mm`/`op`/`fq` are the arm's w8a8_mm, custom op and
     fused_quant module)."""
-    import time
-
     import torch
 
     a = torch.randint(-127, 128, (1, 2048), dtype=torch.int8, device=dev)
@@ -558,10 +773,8 @@ def run_e2e(layers, acts, cases, dev, world, passes):
         us = float(t.item())
     return {"value": round(us, 2), "unit": "us", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "passes": passes,
-            "note": (f"one eager pass over the sweep through int8_linear.w8a8_mm, host copies "
-                     f"included: {len(groups)} groups of consecutive cases, one packed H2D and one "
-                     "packed D2H per group (256-byte aligned slots, counted in the bytes), on "
-                     "their own streams, overlapping each other and the GEMMs")}
+            "note": f"eager sweep through w8a8_mm; {len(groups)} packed H2D + D2H copies per pass, "
+                    "overlapped on their own streams"}
 
 
 def run_standin_tp(dev, rank, world, comm=None):
@@ -589,7 +802,7 @@ def run_standin_tp(dev, rank, world, comm=None):
     return out
 
 
-def run_quantisers(dev):
+def run_quantisers(dev, pk):
     """the fused quantisers, µs per call (graph of 50 calls) and the
     fraction of HBM bandwidth their algorithmic bytes reach.  Timed with the run's
     programmatic-dependent-launch setting and, as `*_no_pdl`, without it: 50 identical
@@ -601,7 +814,6 @@ def run_quantisers(dev):
     from int8_linear import _native
     from int8_linear import fused_quant as fq
 
-    pk = peaks()
     out = {}
     pdl = _native.pdl_enabled()
     g = torch.Generator(device=dev).manual_seed(3)
@@ -647,54 +859,72 @@ def run_standin(dev):
 
 
 # ------------------------------------------------------------------- reference arm
-def cpu_sample_pass(model, rng_seed=0, row_cap=256, col_cap=2048, world=1):
-    """One bounded pass of the sweep through the reference's CPU float64 layer
-    (oracle/gemm.py): rows capped at row_cap and columns at col_cap per GEMM, the time
-    scaled by the full/sampled size (the float64 product is linear in M and N).
-    Returns projected microseconds for the whole sweep."""
-    import numpy as np
+def cpu_operands(model, seed=0):
+    """The sweep's int8 operands on the CPU, generated as config 0 (bf16 N(0,1)
+    activations, N(0,0.02) weights, per-row quantisation; bf16 N(0,0.01) bias): one weight
+    per layer and one activation per (M, K)."""
+    import torch
 
-    from oracle import gemm as og
-    from oracle.numerics import f32_to_bf16_bits
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for name, k, n in layers_for(model):
+        wq, ws = quant_rows_t((torch.randn((n, k), generator=g) * 0.02).to(torch.bfloat16))
+        bias = (torch.randn((n,), generator=g) * 0.01).to(torch.bfloat16)
+        layers.append((name, k, n, wq, ws, bias))
+    acts = {(m, k): quant_rows_t(torch.randn((m, k), generator=g).to(torch.bfloat16))
+            for k in sorted({lay[1] for lay in layers}) for m in M_SWEEP}
+    return layers, acts
 
-    rng = np.random.default_rng(rng_seed)
-    total = 0.0
+
+def cpu_sweep_pass(layers, acts) -> float:
+    """One pass of the whole sweep (every layer, M and bias; full M x N, no sampling)
+    through the reference's CPU float64 layer; returns seconds."""
+    from oracle.gemm import layer_f64_torch
+
+    t0 = time.perf_counter()
     for bias in (False, True):
-        for name, k, n in layers_for(model):
-            n = n // world
-            nc = min(n, col_cap)
-            w_q = rng.integers(-127, 128, (nc, k), dtype=np.int8)
-            w_s = (rng.random((nc, 1), dtype=np.float32) * 1e-3 + 1e-4).astype(np.float32)
-            b = (rng.standard_normal(nc) * 0.01).astype(np.float32) if bias else None
+        for _, k, _, wq, ws, b in layers:
             for m in M_SWEEP:
-                mr = min(m, row_cap)
-                a_q = rng.integers(-127, 128, (mr, k), dtype=np.int8)
-                a_s = (rng.random((mr, 1), dtype=np.float32) * 1e-2).astype(np.float32)
-                t0 = time.perf_counter()
-                acc = og.exact(a_q, w_q)
-                _, ref = og.scaled_ref(acc, a_s, w_s, b)
-                f32_to_bf16_bits(ref.astype(np.float32))
-                dt = time.perf_counter() - t0
-                total += dt * (m / mr) * (n / nc)
-    return total * 1e6
+                a_q, a_s = acts[(m, k)]
+                layer_f64_torch(a_q, a_s, wq, ws, b if bias else None)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(model, passes: int, warmup: int = 1) -> dict:
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    layers, acts = cpu_operands(model)
+    for _ in range(warmup):
+        cpu_sweep_pass(layers, acts)
+    ts = [cpu_sweep_pass(layers, acts) for _ in range(passes)]
+    v = statistics.median(ts) * 1e6
+    return {"value": round(v, 1), "unit": "us", "cores": torch.get_num_threads(), "kind": "port",
+            "cpu": cpu_model(),
+            "sample": f"the whole 96-GEMM sweep (every M, N, bias; no sampling) through the reference's "
+                      f"float64 torch layer (bench/bench_linear.py:164-165), median of {passes} passes"}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return None
-    cores = os.cpu_count() or 1
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    layers, acts = cpu_operands(args.model)
     for _ in range(args.warmup):
-        cpu_sample_pass(args.model, world=1)
+        cpu_sweep_pass(layers, acts)
     t0 = time.perf_counter()
-    vals = [cpu_sample_pass(args.model, world=1) for _ in range(args.steps)]
+    vals = [cpu_sweep_pass(layers, acts) for _ in range(args.steps)]
     wall = time.perf_counter() - t0
-    v = statistics.median(vals)
-    sample = ("one pass of the config-1 sweep (96 GEMMs) through the float64 layer, each GEMM "
-              "on at most 256 rows x 2048 columns, time scaled to the full M x N")
+    v = statistics.median(vals) * 1e6
+    base = {"value": round(v, 1), "unit": "us", "cores": torch.get_num_threads(), "kind": "port",
+            "cpu": cpu_model(),
+            "sample": "each step: the whole 96-GEMM sweep (every M, N, bias; no sampling) through the "
+                      "reference's float64 torch layer (bench/bench_linear.py:164-165); value = median step"}
     return {
         "value": round(v, 1), "ms_per_step": round(wall * 1e3 / args.steps, 2),
-        "cpu_baseline": {"value": round(v, 1), "unit": "us", "cores": cores, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": base,
         "e2e": {"value": round(v, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -765,7 +995,6 @@ def run_reference_triton_child(args):
         t_silu = time_graph(capture(lambda: [rfq.silu_mul_quant(guq, True, True) for _ in range(50)])) / 50
         quant[str(m)] = {"add_rmsnorm_quant_us": round(t_norm, 2), "silu_mul_quant_us": round(t_silu, 2)}
     standin = {}
-    from int8_linear.shapes import SHAPES as RS  # noqa: F401  (the reference's own table)
     for m in STANDIN_BATCHES:
         gg = torch.Generator(device=dev).manual_seed(0)
         x = torch.randn((m, 2048), generator=gg, device=dev).to(torch.bfloat16)
@@ -820,9 +1049,98 @@ def run_reference_triton(args, rank):
     return json.loads(r.stdout.strip().splitlines()[-1])
 
 
+# ------------------------------------------------------------------- profiling cases
+def run_case(args) -> None:
+    """Small, self-contained workloads for profiling one kernel (e.g. under ncu): each runs
+    a few launches (`--iters`) after the first, so `ncu -s <skip> -c <count>` can pick
+    steady-state launches, and keeps the device footprint small.
+
+        --case gemm --shape M,N,K [--config bm,bn[,split[,cluster]]]   one GEMM, 2 weights
+        --case sweep [--model M]                                      every (layer, M) once
+        --case quant --shape M --kind norm|silu|plain                 one quantiser
+        --case standin --shape B                                      stand-in step replays
+    """
+    import torch
+
+    from int8_linear import fused_quant as fq
+    from int8_linear import set_pdl, w8a8_mm
+    from int8_linear.kernel import Config
+
+    set_pdl(not args.no_pdl)
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def ints(shape):
+        return torch.randint(-127, 128, shape, dtype=torch.int8, device="cuda", generator=g)
+
+    if args.case == "gemm":
+        m, n, k = (int(v) for v in args.shape.split(","))
+        cfg = None
+        if args.config:
+            f = [int(v) for v in args.config.split(",")]
+            cfg = Config(f[0], f[1], split=f[2] if len(f) > 2 else 0, cluster=f[3] if len(f) > 3 else 0)
+        a, ws = ints((m, k)), [ints((n, k)) for _ in range(2)]
+        sa = torch.rand((m, 1), device="cuda", generator=g) * 1e-2 + 1e-3
+        sb = torch.rand((n, 1), device="cuda", generator=g) * 1e-3 + 1e-4
+        for i in range(args.iters):
+            w8a8_mm(a, ws[i % 2].t(), sa, sb, torch.bfloat16, config=cfg)
+    elif args.case == "sweep":
+        for _, k, n in layers_for(args.model):
+            w = ints((n, k))
+            sb = torch.rand((n, 1), device="cuda", generator=g) * 1e-3 + 1e-4
+            for m in M_SWEEP:
+                sa = torch.rand((m, 1), device="cuda", generator=g) * 1e-2 + 1e-3
+                w8a8_mm(ints((m, k)), w.t(), sa, sb, torch.bfloat16)
+            torch.cuda.synchronize()
+    elif args.case == "quant":
+        m = int(args.shape)
+        x = torch.randn((m, 2048), device="cuda", generator=g).to(torch.bfloat16)
+        r = torch.randn((m, 2048), device="cuda", generator=g).to(torch.bfloat16)
+        gamma = (1 + 0.1 * torch.randn(2048, device="cuda", generator=g)).to(torch.bfloat16)
+        gu = torch.randn((m, 12288), device="cuda", generator=g).to(torch.bfloat16)
+        for _ in range(args.iters):
+            if args.kind == "norm":
+                fq.add_rmsnorm_quant(x, r, gamma, 1e-6)
+            elif args.kind == "silu":
+                fq.silu_mul_quant(gu, True, True)
+            else:
+                fq.per_token_quant(x)
+    else:
+        from int8_linear.standin import StandinDecoder
+
+        s = StandinDecoder(int(args.shape or 1))
+        gr = s.capture()
+        for _ in range(args.iters):
+            gr.replay()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, "shape": args.shape, "iters": args.iters}), flush=True)
+
+
 # ------------------------------------------------------------------- main
+def short_line(line: dict) -> str:
+    """The final JSON line, dropping optional tables (largest first) if it would exceed
+    LINE_LIMIT bytes."""
+    drop = ["int8_tops_measured", "host_us_per_call", "standin_tp_peer_us_per_layer",
+            "standin_tp_us_per_layer", "quantisers_us"]
+    s = json.dumps(line)
+    for key in drop:
+        if len(s.encode()) <= LINE_LIMIT:
+            break
+        line.pop(key, None)
+        s = json.dumps(line)
+    return s
+
+
+def detail_path(args, world) -> Path:
+    if args.detail:
+        return Path(args.detail)
+    return ROOT / "gpurun_out" / f"bench_detail_n{world}.json"
+
+
 def main():
     args = parse()
+    if args.case:
+        run_case(args)
+        return
     if args.impl == "reference-triton-child":
         # Only the installed reference may provide int8_linear in this process.
         sys.path[:] = [str(REF_INSTALL)] + [p for p in sys.path if Path(p or ".").resolve() != ROOT]
@@ -838,9 +1156,8 @@ def main():
                                    f"{1 if args.model.startswith('qwen') else 2})",
                        "layers": [f"{nm} K={k} N={n}" for nm, k, n in layers_for(args.model)],
                        "M": M_SWEEP, "bias": [False, True],
-                       "l2": (f"cold: {COPIES} launches per case on distinct weight copies from a pool of "
-                              "at least 2x L2 per layer; L2 flushed before each timed window of a "
-                              "case"),
+                       "l2": (f"cold: {COPIES} launches per case on distinct weight copies from a pool "
+                              "of at least 2x L2 per layer"),
                        "parallelism": f"column-parallel N/{world}" if world > 1 else "single GPU",
                        "pdl": not args.no_pdl}}
     if args.impl == "reference-triton":
@@ -855,7 +1172,6 @@ def main():
             print(json.dumps(line), flush=True)
         return
 
-    import numpy as np  # noqa: F401  (imported before CUDA so a spawned pool would be safe)
     import torch
     import torch.distributed as dist
 
@@ -866,18 +1182,21 @@ def main():
     set_pdl(not args.no_pdl)  # inference weights are read-only: let kernels overlap
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-    res = run_ours(args, world, rank, dev)
+    line, detail = run_ours(args, world, rank, dev)
     cpu = None
     if world == 1 and rank == 0:
-        v = cpu_sample_pass(args.model)
-        cpu = {"value": round(v, 1), "unit": "us", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": "one pass of the sweep through the float64 layer (oracle/gemm.py), each "
-                         "GEMM on at most 256 rows x 2048 columns, time scaled to the full M x N"}
+        cpu = cpu_baseline(args.model, passes=3)
     if rank == 0:
-        line = dict(base, dtype="i8", cpu_baseline=cpu, **res)
-        print(json.dumps(line), flush=True)
+        dpath = detail_path(args, world)
+        dpath.parent.mkdir(parents=True, exist_ok=True)
+        full = dict(base, dtype="i8", cpu_baseline=cpu, **line, **detail)
+        dpath.write_text(json.dumps(full, indent=1) + "\n")
+        out = dict(base, dtype="i8", cpu_baseline=cpu, **line)
+        out["detail"] = os.path.relpath(dpath, ROOT)
+        s = short_line(out)
+        print(s, flush=True)
         if args.out:
-            Path(args.out).write_text(json.dumps(line, indent=1) + "\n")
+            Path(args.out).write_text(s + "\n")
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

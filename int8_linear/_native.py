@@ -128,15 +128,28 @@ def check(code: int) -> None:
     raise RuntimeError(f"int8_linear native call failed ({code}): {msg}")
 
 
+# Called when the status word shows a kernel gave up a wait, and by clear_status():
+# the GEMM module registers the re-zeroing of its split-K workspaces here.
+STATUS_HOOKS: list = []
+
+
 def read_status() -> int:
-    """Synchronise the device and return the kernels' status word (0 = clean)."""
+    """Synchronise the device and return the kernels' status word (0 = clean).  A
+    non-zero word also re-zeroes the cached split-K workspaces (STATUS_HOOKS): a kernel
+    that gave up a wait may have left partial sums in them."""
     v = _i32(0)
     check(load().i8l_read_status(ctypes.byref(v)))
+    if v.value:
+        for hook in STATUS_HOOKS:
+            hook()
     return int(v.value)
 
 
 def clear_status() -> None:
+    """Reset the status word and re-zero the cached split-K workspaces."""
     check(load().i8l_clear_status())
+    for hook in STATUS_HOOKS:
+        hook()
 
 
 def set_pdl(enable: bool) -> None:

@@ -180,6 +180,7 @@ def choose_config(m: int, n: int, k: int) -> Config:
 
 _DTYPE_CODE = {torch.bfloat16: _native.BF16, torch.float16: _native.F16, torch.float32: _native.F32}
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_capture_workspaces: dict[int, torch.Tensor] = {}
 _tiles: dict[Config, _native.I8LTile] = {}
 # The current stream's raw handle without building a torch.cuda.Stream object (the host
 # cost of an eager call is a few microseconds, so each one counts).
@@ -201,15 +202,53 @@ def _tile_of(cfg: Config) -> _native.I8LTile:
     return tile
 
 
+def _zeroed(index: int) -> torch.Tensor:
+    return torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8, device=torch.device("cuda", index))
+
+
 def workspace(device: torch.device | int, stream: int) -> torch.Tensor:
-    """The zero-filled split-K workspace for this device and stream (allocated once)."""
+    """The zero-filled split-K workspace for calls on this device and stream.
+
+    Eager calls get one workspace per (device, stream), allocated on the first call.
+    Calls captured into a CUDA graph share one workspace per device, allocated and
+    zeroed (together with the first eager one) outside any capture: a buffer created
+    inside a capture would come from that graph's private pool, and its zero fill would
+    be a node of that one graph, done only when that graph is replayed.  So the first
+    GEMM on a device must not be inside a capture (a warm-up call first, as graph capture
+    needs anyway), and graphs captured on one device must not be replayed concurrently
+    on different streams.  Kernels leave a workspace zeroed; reset_workspaces() zeroes
+    them all again after a kernel gave up a wait (i8l_read_status)."""
     index = device if isinstance(device, int) else device.index
     key = (index, stream)
     ws = _workspaces.get(key)
-    if ws is None:
-        ws = _workspaces[key] = torch.zeros(WORKSPACE_BYTES, dtype=torch.uint8,
-                                            device=torch.device("cuda", index))
+    if ws is not None:
+        return ws
+    if torch.cuda.is_current_stream_capturing():
+        ws = _capture_workspaces.get(index)
+        if ws is None:
+            raise RuntimeError(
+                f"the first int8_linear GEMM on cuda:{index} is being captured into a CUDA graph: "
+                "make one call outside the capture first (a warm-up), so the split-K workspace "
+                "is allocated and zeroed before it")
+    else:
+        if index not in _capture_workspaces:
+            _capture_workspaces[index] = _zeroed(index)
+        ws = _zeroed(index)
+    _workspaces[key] = ws
     return ws
+
+
+def reset_workspaces() -> None:
+    """Zero every cached split-K workspace again (and wait for it).  Kernels leave their
+    slots and counters zeroed when they finish; one whose bounded wait gave up may not
+    have, and later split-K calls would then add into stale sums."""
+    for ws in {id(w): w for w in (*_workspaces.values(), *_capture_workspaces.values())}.values():
+        with torch.cuda.device(ws.device):
+            ws.zero_()
+            torch.cuda.synchronize()
+
+
+_native.STATUS_HOOKS.append(reset_workspaces)
 
 
 def _aligned_rows(t: torch.Tensor) -> torch.Tensor:

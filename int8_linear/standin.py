@@ -74,29 +74,42 @@ class StandinDecoder:
         self.graph: torch.cuda.CUDAGraph | None = None
         self.out: torch.Tensor | None = None
 
-    def step(self) -> torch.Tensor:
+    def step(self, record: list | None = None) -> torch.Tensor:
+        """One decode step.  With `record` (a list), every op appends (layer, op name,
+        inputs, outputs), so a test can check each op on its own inputs."""
         cfg = self.configs.get
+
+        def rec(i, name, ins, outs):
+            if record is not None:
+                record.append((i, name, ins, outs))
+            return outs
+
         res = self.x
-        q, s, _ = add_rmsnorm_quant(self.x, None, self.w, EPS)
+        q, s, _ = rec(-1, "norm", (self.x, None, self.w), add_rmsnorm_quant(self.x, None, self.w, EPS))
         h = None
         for i, layer in enumerate(self.layers):
             if i:
-                q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
+                q, s, res = rec(i, "norm", (h, res, self.w), add_rmsnorm_quant(h, res, self.w, EPS))
             lin = layer["qkv_proj"]
-            qkv = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("qkv_proj"))
+            qkv = rec(i, "qkv_proj", (q, s, lin),
+                      w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("qkv_proj")))
             lin = layer["o_proj"]
             if self.fuse_o_proj:
-                h = w8a8_mm_quant_act(qkv[:, :HIDDEN], lin.w_t, lin.scale, torch.bfloat16,
-                                      config=cfg("o_proj"))
+                h = rec(i, "o_proj_quant_act", (qkv[:, :HIDDEN], lin),
+                        w8a8_mm_quant_act(qkv[:, :HIDDEN], lin.w_t, lin.scale, torch.bfloat16,
+                                          config=cfg("o_proj")))
             else:
-                q, s = per_token_quant(qkv[:, :HIDDEN])
-                h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("o_proj"))
-            q, s, res = add_rmsnorm_quant(h, res, self.w, EPS)
+                q, s = rec(i, "quant", (qkv[:, :HIDDEN],), per_token_quant(qkv[:, :HIDDEN]))
+                h = rec(i, "o_proj", (q, s, lin),
+                        w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("o_proj")))
+            q, s, res = rec(i, "post_norm", (h, res, self.w), add_rmsnorm_quant(h, res, self.w, EPS))
             lin = layer["gate_up_proj"]
-            gu = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("gate_up_proj"))
-            q, s = silu_mul_quant(gu)
+            gu = rec(i, "gate_up_proj", (q, s, lin),
+                     w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("gate_up_proj")))
+            q, s = rec(i, "silu_mul_quant", (gu,), silu_mul_quant(gu))
             lin = layer["down_proj"]
-            h = w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("down_proj"))
+            h = rec(i, "down_proj", (q, s, lin),
+                    w8a8_mm(q, lin.w_t, s, lin.scale, torch.bfloat16, config=cfg("down_proj")))
         return h
 
     def capture(self) -> torch.cuda.CUDAGraph:

@@ -44,6 +44,20 @@ def scaled_ref(acc: np.ndarray, sa: np.ndarray, sb: np.ndarray,
     return term, ref
 
 
+def layer_f64_torch(a_q, a_s, w_q, w_s, bias=None, out_dtype=None):
+    """The reference's float64 layer in torch, as bench/bench_linear.py:164-165 writes it:
+    term = (A_q.double() @ W_q.double().t()) * a_s.double() * w_s.double().t(), plus
+    bias.double(); rounded to out_dtype (bf16 unless given).  a_q int8 [M, K], a_s
+    float32 [M, 1], w_q int8 [N, K], w_s float32 [N, 1], bias [N] or None, all torch
+    CPU tensors.  This is the CPU path the benchmark times as the reference; its
+    float64 values equal `scaled_ref` on the same inputs (tests/test_oracle_golden.py)."""
+    import torch
+
+    term = (a_q.double() @ w_q.double().t()) * a_s.double() * w_s.double().t()
+    ref = term + bias.double() if bias is not None else term
+    return ref.to(out_dtype or torch.bfloat16)
+
+
 def epilogue_f32(acc: np.ndarray, sa: np.ndarray, sb: np.ndarray,
                  bias: np.ndarray | None = None) -> np.ndarray:
     """The kernel's epilogue in float32, each step rounded (kernel.py:109-120):

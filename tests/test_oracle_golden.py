@@ -118,3 +118,18 @@ def test_compare_int8_catches_a_planted_error():
     many[:, :100] = 1
     assert not oq.compare_int8(many, s, q, s).ok()
     assert oq.compare_int8(q, s * (1 + 1e-4), q, s).scale_rel > 1e-5
+
+
+@pytest.mark.parametrize("use_bias", [False, True])
+def test_torch_float64_layer_is_the_numpy_layer(use_bias):
+    """The torch restatement the benchmark times as the reference's CPU path
+    (bench/bench_linear.py:164-165) gives the numpy oracle's float64 values, and its bf16
+    output is the float64 layer rounded once."""
+    a, w, sa, sb, bias = recipes.scaled_case(torch.bfloat16, True, True, use_bias)
+    acc = og.exact(a.numpy(), w.numpy())
+    _, ref = og.scaled_ref(acc, sa.numpy(), sb.numpy(), f32(bias) if use_bias else None)
+    got64 = og.layer_f64_torch(a, sa.reshape(-1, 1), w, sb.reshape(-1, 1),
+                               bias if use_bias else None, torch.float64)
+    assert np.array_equal(got64.numpy(), ref)
+    got = og.layer_f64_torch(a, sa.reshape(-1, 1), w, sb.reshape(-1, 1), bias if use_bias else None)
+    assert torch.equal(got, torch.from_numpy(ref).to(torch.bfloat16))
