@@ -636,8 +636,7 @@ def run_ours(args, world, rank, dev):
         "standin_tp_us_per_layer": standin_tp, "standin_tp_peer_us_per_layer": standin_tp_peer,
         "host_us_per_call": host, "clocks": clocks.summary(), "gpu_launches": launches,
     }
-    detail = {"per_shape": per_shape, "l2_warm_us": warm, "quantisers": quant, "ties": ties,
-              "int8_tops_measured": peak}
+    detail = {"per_shape": per_shape, "l2_warm_us": warm, "quantisers": quant, "ties": ties}
     return line, detail
 
 
@@ -1189,7 +1188,7 @@ def main():
     if rank == 0:
         dpath = detail_path(args, world)
         dpath.parent.mkdir(parents=True, exist_ok=True)
-        full = dict(base, dtype="i8", cpu_baseline=cpu, **line, **detail)
+        full = {**base, "dtype": "i8", "cpu_baseline": cpu, **line, **detail}
         dpath.write_text(json.dumps(full, indent=1) + "\n")
         out = dict(base, dtype="i8", cpu_baseline=cpu, **line)
         out["detail"] = os.path.relpath(dpath, ROOT)

@@ -53,8 +53,13 @@ extern "C" {
  *                0 = the library's choice; 1 = whole tiles; 2 = stream-K over the SMs,
  *                partial sums reduced through the workspace; 3 = cluster split-K:
  *                the CTAs of a thread-block cluster split one tile's K and reduce over
- *                distributed shared memory (swap_ab tiles of up to 64 tokens; no
- *                workspace);
+ *                distributed shared memory (swap_ab tiles of up to 256 tokens, as the
+ *                partial sums fit the leader's ring; no workspace); 4 = CTA pairs
+ *                (cta_group::2) on 128 x 256 tiles; 5 = CUDA-core tiles for batches of
+ *                at most tok_tile in {1, 2, 4, 8} tokens (w_tile 0, swap_ab 0): each CTA
+ *                owns whole output columns (dp4a int8 dot products, no split-K, no
+ *                workspace), its weight rows streamed into shared memory by 1-D bulk
+ *                copies; `ctas` and `stages` apply;
  *   cluster:     CTAs per cluster for split = 3 (0 = the library's choice, <= 8);
  *   store:       output path: 0 = the library's choice, 1 = TMA stores through
  *                shared memory, 2 = plain stores;

@@ -33,6 +33,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "epilogue.cuh"
 #include "internal.h"
 
 namespace i8l {
@@ -199,60 +200,6 @@ __device__ __forceinline__ void tile_coords(const GemmArgs &a, int t, int &tx,
 __device__ __forceinline__ void cta_tile(const GemmArgs &a, int t, int &tx, int &ty) {
   tile_coords(a, t, tx, ty);
   if (a.pair) tx = 2 * tx + static_cast<int>(blockIdx.x & 1u);
-}
-
-__device__ __forceinline__ float load_scalar_f(const void *p, int dtype, long long i) {
-  switch (dtype) {
-    case I8L_BF16:
-      return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
-    case I8L_F16:
-      return __half2float(static_cast<const __half *>(p)[i]);
-    default:
-      return static_cast<const float *>(p)[i];
-  }
-}
-
-// The reference's epilogue order: float(acc) * sa, then * sb, then + bias, each
-// rounded in fp32 (no contraction into an FMA), then one rounding to the output.
-__device__ __forceinline__ float dequant(int acc, float sa, float sb, float bias,
-                                         bool has_bias) {
-  float v = __int2float_rn(acc);
-  v = __fmul_rn(v, sa);
-  v = __fmul_rn(v, sb);
-  if (has_bias) v = __fadd_rn(v, bias);
-  return v;
-}
-
-// Storage bits of one output value.
-__device__ __forceinline__ uint32_t out_bits16(int dtype, float v) {
-  if (dtype == I8L_BF16) {
-    __nv_bfloat16 h = __float2bfloat16_rn(v);
-    return *reinterpret_cast<uint16_t *>(&h);
-  }
-  __half h = __float2half_rn(v);
-  return *reinterpret_cast<uint16_t *>(&h);
-}
-
-__device__ __forceinline__ uint32_t out_bits32(int dtype, int acc, float v) {
-  return dtype == I8L_I32 ? static_cast<uint32_t>(acc) : __float_as_uint(v);
-}
-
-__device__ __forceinline__ void store_elem(void *out, int dtype, long long idx,
-                                           int acc, float v) {
-  switch (dtype) {
-    case I8L_BF16:
-      static_cast<__nv_bfloat16 *>(out)[idx] = __float2bfloat16_rn(v);
-      break;
-    case I8L_F16:
-      static_cast<__half *>(out)[idx] = __float2half_rn(v);
-      break;
-    case I8L_F32:
-      static_cast<float *>(out)[idx] = v;
-      break;
-    default:
-      static_cast<int *>(out)[idx] = acc;
-      break;
-  }
 }
 
 // Everything one epilogue thread needs about the current tile.
@@ -1423,6 +1370,17 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   DeviceInfo di;
   int e = device_info(&di);
   if (e) return e;
+  if (user && user->split == 5) {
+    // CUDA-core tiles (gemv_sm100.cu): whole output columns per CTA, no workspace.
+    GemvPlan gp;
+    if ((e = gemv_plan(M, N, K, user, &gp))) return e;
+    *p = Plan{};
+    p->tile = *user;
+    p->tile.stages = gp.stages;
+    p->tile.ctas = gp.ctas;
+    p->ctas = gp.ctas;
+    return I8L_OK;
+  }
   i8l_tile t;
   const bool auto_tile = user == nullptr || (user->tok_tile == 0 && user->w_tile == 0);
   if (auto_tile) {
@@ -1508,8 +1466,8 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
     }
   }
   if (split == 3) {
-    if (!narrow && (!t.swap_ab || p->tn > 64))
-      return set_error(I8L_ENOTSUP, "cluster split-K takes swap_ab tiles of at most 64 tokens");
+    if (!narrow && !t.swap_ab)
+      return set_error(I8L_ENOTSUP, "cluster split-K takes swap_ab tiles or narrow 128 x 256 tiles");
     // The leader's operand ring receives (cluster-1) partial-sum slots: TN x 128 int32
     // (swap_ab tiles), or M token rows x TN int32 (narrow tiles).
     const long long ring = static_cast<long long>(t.stages) * (x_rows * kBK + p->tn * kBK);
@@ -1657,6 +1615,13 @@ static int gemm_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, 
     if ((!sa && !aq) || !sb) return set_error(I8L_EINVAL, "NULL scale pointer");
     if (bias && (bias_dtype < I8L_BF16 || bias_dtype > I8L_F32))
       return set_error(I8L_ENOTSUP, "bias dtype code %d not supported", bias_dtype);
+  }
+  if (tile && tile->split == 5) {
+    if (aq)
+      return set_error(I8L_ENOTSUP, "fused activation quantisation needs direct activation loads, "
+                                    "which CUDA-core tiles (split 5) do not have");
+    return gemv_run(A, lda, W, ldw, sa, sa_per_row, sb, sb_per_col, bias, bias_dtype, out, out_dtype,
+                    ldc, M, N, K, tile, stream);
   }
   Plan p;
   int e = make_plan(M, N, K, tile, &p);

@@ -29,6 +29,21 @@ int device_info(DeviceInfo *out);
 // Device pointer of the status word kernels set when a bounded wait gives up.
 int *status_ptr();
 
+// The CUDA-core GEMM for decode batches of <= 8 tokens (split mode 5, gemv_sm100.cu).
+struct GemvPlan {
+  int mt;          // tokens the kernel variant holds (1, 2, 4, 8)
+  int ctas;        // CTAs, each owning a contiguous range of output columns
+  int max_rows;    // most columns one CTA owns
+  int stage_rows;  // weight rows per shared-memory stage
+  int stages;      // ring depth
+  size_t smem;     // dynamic shared memory per CTA
+};
+int gemv_plan(int M, int N, int K, const i8l_tile *tile, GemvPlan *p);
+int gemv_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, const float *sa,
+             int32_t sa_per_row, const float *sb, int32_t sb_per_col, const void *bias,
+             int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
+             int32_t K, const i8l_tile *tile, void *stream);
+
 // Whether kernels are launched with programmatic stream serialisation (PDL).
 bool pdl_enabled();
 

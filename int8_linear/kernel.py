@@ -31,6 +31,7 @@ from int8_linear._native import NotSupported
 
 TUNED_PATH = Path(__file__).with_name("tuned_configs.json")
 TOKEN_TILES = (16, 32, 64, 128, 256)
+GEMV_TOKENS = (1, 2, 4, 8)   # token counts of the CUDA-core tiles (split 5)
 # Split-K workspace kept per (device, stream); kernels leave it zero-filled.  The
 # largest plan needs (SMs - 1) slots of 128 x 256 int32 plus counters, ~19 MB on
 # 148 SMs, so one allocation covers every call.
@@ -56,10 +57,15 @@ class Config:
             choice gives the same bits: 0 the library's choice, 1 whole tiles, 2
             stream-K over the SMs (reduced in a workspace), 3 cluster split-K (the CTAs
             of a thread-block cluster split a tile's K and reduce over distributed
-            shared memory; swap_ab tiles of at most 64 tokens, or, without swap_ab, narrow
+            shared memory; swap_ab tiles, as many CTAs as the leader's ring holds partial
+            sums for (up to 4 at 128 tokens, 2 at 256), or, without swap_ab, narrow
             128 x 256 tiles for batches of <= 16 tokens: the weight on the MMA's N side,
             256 weight rows per MMA instruction), 4 CTA pairs (two SMs
-            per 256 x 256 tile with 256-row tcgen05 MMAs; 128 x 256 tiles, no swap_ab).
+            per 256 x 256 tile with 256-row tcgen05 MMAs; 128 x 256 tiles, no swap_ab),
+            5 CUDA-core tiles for decode batches of at most 8 tokens: bm in (1, 2, 4, 8)
+            is the most tokens, bn = 0; each CTA owns whole output columns (int8 dot
+            products with dp4a, no split-K), its weight rows streamed into shared memory
+            by 1-D bulk copies that start before the dependency wait.
     ctas    persistent CTAs, 0 for one per SM.
     cluster CTAs per cluster for split=3, 0 for the library's choice.
     store   output path: 0 the library's choice, 1 TMA stores, 2 plain stores.
@@ -83,10 +89,14 @@ class Config:
 
     @property
     def swapped(self) -> bool:
+        if self.split == 5:
+            return False
         return self.bm != 128 if self.swap_ab is None else bool(self.swap_ab)
 
     @property
     def name(self) -> str:
+        if self.split == 5:
+            return f"gemv m{self.bm} s{self.stages}" + (f" c{self.ctas}" if self.ctas else "")
         tail = (" swap" if self.swapped else "") + {0: "", 1: " whole", 2: " sk", 3: " cl", 4: " pair"}.get(
             self.split, f" split{self.split}")
         tail += str(self.cluster) if self.split == 3 and self.cluster else ""
@@ -97,6 +107,10 @@ class Config:
 
     def check(self) -> None:
         """Raise NotSupported unless a B200 kernel exists for this tiling."""
+        if self.split == 5:
+            if self.bm not in GEMV_TOKENS or self.bn != 0 or self.stages < 0 or self.ctas < 0:
+                raise NotSupported(f"{self.name}: CUDA-core tiles take bm in {GEMV_TOKENS}, bn 0")
+            return
         if self.bk != 128 or self.warps != 6:
             raise NotSupported(f"{self.name}: B200 tiles use bk=128 and 6 warps")
         if self.swapped:
@@ -104,7 +118,7 @@ class Config:
                 raise NotSupported(f"{self.name}: swap_ab tiles are bm in {TOKEN_TILES} x bn 128")
         elif self.bm != 128 or self.bn not in (128, 256):
             raise NotSupported(f"{self.name}: tiles are bm 128 x bn in (128, 256)")
-        if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1, 2, 3, 4):
+        if self.stages < 0 or self.stages == 1 or self.group_m < 1 or self.split not in (0, 1, 2, 3, 4, 5):
             raise NotSupported(f"{self.name}: bad stages/group_m/split")
         if self.store not in (0, 1, 2) or self.act not in (0, 1, 2):
             raise NotSupported(f"{self.name}: store and act must be 0, 1 or 2")
@@ -112,13 +126,16 @@ class Config:
             raise NotSupported(f"{self.name}: direct activation loads take swap_ab tiles")
         if self.split == 3 and not 0 <= self.cluster <= 8:
             raise NotSupported(f"{self.name}: clusters hold at most 8 CTAs")
-        if self.split == 3 and (self.bm > 64 if self.swapped else self.bn != 256):
-            raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles of <= 64 tokens "
+        if self.split == 3 and not self.swapped and self.bn != 256:
+            raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles "
                                "or narrow 128 x 256 tiles (batches of <= 16 tokens)")
         if self.split == 4 and (self.swapped or self.bn != 256):
             raise NotSupported(f"{self.name}: CTA pairs take 128 x 256 tiles without swap_ab")
 
     def as_tile(self) -> _native.I8LTile:
+        if self.split == 5:
+            return _native.I8LTile(swap_ab=0, tok_tile=self.bm, w_tile=0, stages=self.stages,
+                                   ctas=self.ctas, group=1, split=5)
         return _native.I8LTile(
             swap_ab=1 if self.swapped else 0, tok_tile=self.bm if self.swapped else 128,
             w_tile=128 if self.swapped else self.bn, stages=self.stages, ctas=self.ctas,
@@ -127,7 +144,9 @@ class Config:
 
 
 def default_config(m: int, n: int, k: int) -> Config:
-    """The untuned choice.  Decode batches (M <= 256) put the weight on the 128-row
+    """The untuned choice.  Batches of at most 4 tokens, and of at most 8 on weights up to
+    16 MB, take the CUDA-core tiles (split 5; measured faster than every tensor-core tiling
+    there on B200).  Other decode batches (M <= 256) put the weight on the 128-row
     MMA side and the tokens on the narrow side, the smallest token tile that holds
     M; larger batches use 128 x 256 tiles.  The library then splits K when whole
     tiles would leave SMs idle: inside thread-block clusters for decode tiles, by
@@ -136,8 +155,8 @@ def default_config(m: int, n: int, k: int) -> Config:
     instead: 256 weight rows per MMA, K split over a cluster of up to 8 CTAs with at
     least two 128-wide k-blocks each (measured faster there on B200; larger weights
     have too few 256-row tiles to fill the SMs)."""
-    if m <= 2 and 1024 <= k <= 6144 and n <= 8192:
-        return Config(128, 256, split=3, cluster=min(8, k // 256))
+    if m <= 4 or (m <= 8 and n * k <= 16 << 20):
+        return Config(next(t for t in GEMV_TOKENS if t >= m), 0, split=5)
     if m <= 256:
         return Config(next(t for t in TOKEN_TILES if t >= m), 128)
     # Prefill: the wider tile unless the narrower one fills the SMs clearly better.
@@ -169,12 +188,21 @@ def tuned_config(m: int, n: int, k: int) -> Config | None:
 _chosen: dict[tuple[int, int, int, int], Config] = {}
 
 
+def _fits(cfg: Config, m: int, n: int, k: int) -> Config:
+    """cfg adapted to M when a table bucket's tiling cannot hold it: a CUDA-core tile for
+    fewer tokens than M takes the next larger token count (up to 8), else the default."""
+    if cfg.split == 5 and m > cfg.bm:
+        bigger = [t for t in GEMV_TOKENS if t >= m]
+        return replace(cfg, bm=bigger[0]) if bigger else default_config(m, n, k)
+    return cfg
+
+
 def choose_config(m: int, n: int, k: int) -> Config:
     """tuned_config, else default_config, remembered per device and shape."""
     key = (torch.cuda.current_device(), m, n, k)
     cfg = _chosen.get(key)
     if cfg is None:
-        cfg = _chosen[key] = tuned_config(m, n, k) or default_config(m, n, k)
+        cfg = _chosen[key] = _fits(tuned_config(m, n, k) or default_config(m, n, k), m, n, k)
     return cfg
 
 

@@ -33,7 +33,7 @@ import torch
 
 from int8_linear import _native
 from int8_linear import fused_quant as fq
-from int8_linear.kernel import TOKEN_TILES, TUNED_PATH, Config, NotSupported, default_config, w8a8_mm
+from int8_linear.kernel import GEMV_TOKENS, TOKEN_TILES, TUNED_PATH, Config, NotSupported, default_config, w8a8_mm
 from int8_linear.shapes import SHAPES
 
 M_DEFAULT = [1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 1024, 4096]
@@ -78,6 +78,13 @@ def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
             if m <= 32:   # plain versus TMA stores for the few output rows
                 out += [Config(tn, 128, split=3, cluster=c, store=1) for c in (2, 4)]
                 out += [Config(tn, 128, split=1, store=1), Config(tn, 128, split=2, store=2)]
+    if m <= 8:    # CUDA-core tiles: whole output columns per CTA, no split-K
+        mt = next(t for t in GEMV_TOKENS if t >= m)
+        out += [Config(mt, 0, split=5), Config(mt, 0, split=5, ctas=2 * sms),
+                Config(mt, 0, split=5, stages=16)]
+    if 64 < m <= 256:   # cluster split-K on the 128- and 256-token swap tiles
+        tn = next(t for t in TOKEN_TILES if t >= m)
+        out += [Config(tn, 128, swap_ab=True, split=3, cluster=c) for c in (2, 3, 4)]
     if m >= 64:
         for bn in (128, 256):
             out += [Config(128, bn, split=1), Config(128, bn, split=2)]

@@ -17,13 +17,25 @@ def test_default_config_is_a_valid_tiling(m, k, n):
     default_config(m, n, k).check()
 
 
-def test_one_and_two_token_batches_default_to_narrow_tiles_on_moderate_weights():
+def test_small_batches_default_to_cuda_core_tiles():
     cfg = default_config(1, 4096, 2048)
-    assert (cfg.bm, cfg.bn, cfg.split, cfg.cluster, cfg.swapped) == (128, 256, 3, 8, False)
-    assert default_config(2, 2048, 1024).cluster == 4            # two k-blocks per CTA
-    assert default_config(1, 12288, 2048).swapped                # too few 256-row tiles
-    assert default_config(1, 4096, 14336).swapped                # long K: swap tiles
-    assert default_config(3, 4096, 2048).swapped                 # beyond two tokens: swap tiles
+    assert (cfg.bm, cfg.bn, cfg.split) == (1, 0, 5)
+    assert default_config(3, 4096, 2048).bm == 4                   # the smallest token count >= M
+    assert default_config(4, 28672, 4096).split == 5               # up to 4 tokens on any weight
+    assert default_config(8, 4096, 2048).split == 5                # 8 tokens on weights <= 16 MB
+    assert default_config(8, 12288, 2048).swapped                  # 8 tokens on a 25 MB weight
+    assert default_config(9, 4096, 2048).swapped                   # beyond 8 tokens: tensor cores
+
+
+def test_choose_config_fits_a_cuda_core_bucket_to_the_batch(monkeypatch):
+    from int8_linear import kernel
+
+    monkeypatch.setattr(kernel.torch.cuda, "current_device", lambda: 0)
+    monkeypatch.setattr(kernel, "tuned_config", lambda m, n, k: Config(4, 0, split=5))
+    monkeypatch.setattr(kernel, "_chosen", {})
+    assert kernel.choose_config(3, 4096, 2048).bm == 4
+    assert kernel.choose_config(5, 4096, 2048) == Config(8, 0, split=5)       # bumped to 8 tokens
+    assert kernel.choose_config(12, 4096, 2048) == default_config(12, 4096, 2048)
 
 
 def test_tuned_table_entries_are_valid_tilings():
@@ -83,3 +95,19 @@ def test_fused_activation_entry_validates_before_touching_a_gpu():
         w8a8_mm_quant_act(torch.zeros((2, 64)), w, sb)                     # fp32 activation
     with pytest.raises(ValueError, match="cannot multiply"):
         w8a8_mm_quant_act(torch.zeros((2, 48), dtype=torch.bfloat16), w, sb)
+
+
+def test_cuda_core_tiles_are_valid_configs():
+    from int8_linear import Config, NotSupported
+
+    cfg = Config(4, 0, split=5, ctas=100)
+    cfg.check()
+    assert not cfg.swapped and cfg.name == "gemv m4 s0 c100"
+    t = cfg.as_tile()
+    assert (t.swap_ab, t.tok_tile, t.w_tile, t.split, t.ctas) == (0, 4, 0, 5, 100)
+    for bad in (Config(3, 0, split=5), Config(16, 0, split=5), Config(8, 128, split=5)):
+        with pytest.raises(NotSupported):
+            bad.check()
+    # cluster split-K now takes the wider token tiles too
+    Config(128, 128, swap_ab=True, split=3, cluster=4).check()
+    Config(256, 128, split=3, cluster=2).check()

@@ -296,7 +296,7 @@ def test_empty_batch():
 
 def test_choose_config_is_per_shape():
     decode, prefill = choose_config(1, 4096, 2048), choose_config(4096, 4096, 2048)
-    assert decode.swapped or decode.split == 3   # swap_ab or narrow decode tiles
+    assert decode.swapped or decode.split in (3, 5)   # swap_ab, narrow or CUDA-core decode tiles
     assert not prefill.swapped and prefill.split != 3
 
 
@@ -357,4 +357,82 @@ def test_untuned_one_and_two_token_batches_take_narrow_tiles_bit_exact(m, k, n):
     want = exact(a, w)
     assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True)), want)
     got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias)
+    assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), "bf16"))
+
+
+GEMV_SHAPES = [(16, 1), (48, 77), (2048, 4096), (6144, 2048), (2048, 12288), (14336, 4096), (1040, 1000),
+               (4096, 28672)]
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("k,n", GEMV_SHAPES)
+def test_cuda_core_tiles_bit_exact(m, k, n):
+    """CUDA-core tiles (split 5): whole output columns per CTA, dp4a dot products; the
+    int32 product exact and every output dtype bit-exact against the fp32 epilogue."""
+    a, w = ints((m, k), 90 + m), ints((n, k), 91 + k)
+    g = torch.Generator().manual_seed(92)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    cfg = Config(next(t for t in (1, 2, 4, 8) if t >= m), 0, split=5)
+    want = exact(a, w)
+    assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), want)
+    for dt, code in ((torch.bfloat16, "bf16"), (torch.float16, "f16"), (torch.float32, "f32")):
+        got = w8a8_mm(a, w.t(), sa, sb, dt, bias, config=cfg)
+        assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), code)), dt
+
+
+@pytest.mark.parametrize("cfg", [Config(8, 0, split=5, ctas=1), Config(4, 0, split=5, ctas=7),
+                                 Config(8, 0, split=5, ctas=300), Config(2, 0, split=5, stages=1),
+                                 Config(4, 0, split=5, stages=2), Config(8, 0, split=5, stages=3, ctas=37)],
+                         ids=lambda c: c.name)
+def test_cuda_core_tiles_under_other_grids(cfg):
+    """Fewer and more CTAs than SMs (each owning a contiguous column range) and short rings
+    (stages refilled many times): same bits."""
+    m, k, n = min(cfg.bm, 3), 6144, 4100
+    a, w = ints((m, k), 93), ints((n, k), 94)
+    got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
+    assert np.array_equal(np_(got), exact(a, w))
+
+
+def test_cuda_core_tiles_on_strided_operands():
+    """A weight and an activation that are column slices of wider buffers (row strides
+    larger than K: one bulk copy per weight row) and an output with a wider row stride."""
+    m, k, n = 5, 2048, 1000
+    a_full, w_full = ints((m, k + 64), 95), ints((n, k + 32), 96)
+    a, w = a_full[:, :k], w_full[:, :k]
+    out_full = torch.full((m, n + 8), float("nan"), dtype=torch.bfloat16, device="cuda")
+    out = out_full[:, :n]
+    sa, sb = torch.full((m, 1), 1e-2, device="cuda"), torch.full((n, 1), 1e-3, device="cuda")
+    w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, config=Config(8, 0, split=5), out=out)
+    want = exact(a.contiguous(), w.contiguous())
+    assert np.array_equal(bits(out), to_bits(og.epilogue_f32(want, np_(sa), np_(sb)), "bf16"))
+    assert bool(out_full[:, n:].isnan().all())    # nothing written past the rows
+
+
+def test_cuda_core_tiles_decline_larger_batches():
+    with pytest.raises(NotSupported):
+        w8a8_mm(ints((9, 2048), 1), ints((64, 2048), 2).t(), one(), one(), config=Config(8, 0, split=5))
+
+
+@pytest.mark.parametrize("m", [65, 100, 128, 200, 256])
+@pytest.mark.parametrize("k,n", [(2048, 4096), (6144, 2048), (2048, 12288), (1040, 1000)])
+@pytest.mark.parametrize("cluster", [2, 3, 4])
+def test_cluster_split_wide_token_tiles(m, k, n, cluster):
+    """Cluster split-K on 128- and 256-token swap tiles: partial sums of 64 or 128 KB per
+    contributor into the leader's ring; declined when they do not fit."""
+    a, w = ints((m, k), 100 + m), ints((n, k), 101)
+    g = torch.Generator().manual_seed(102)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    cfg = Config(tok_tile(m), 128, swap_ab=True, split=3, cluster=cluster)
+    want = exact(a, w)
+    try:
+        got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
+    except NotSupported as e:
+        assert "cluster size" in str(e) and tok_tile(m) == 256, e
+        return
+    assert np.array_equal(np_(got), want)
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=cfg)
     assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), "bf16"))
