@@ -119,9 +119,11 @@ int i8l_w8a8_mm(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw,
  * i8l_w8a8_mm bit for bit, with one launch instead of two and no int8 copy of X in
  * HBM.  Other arguments as i8l_w8a8_mm (there is no sa).
  *
- * Only tiles that use direct activation loads take it: swap_ab, M <= tok_tile, one
- * tile or cluster segment per CTA, at most `stages` k-blocks per CTA (tile->act 0 or
- * 2); any other returns I8L_ENOTSUP and the caller quantises separately.
+ * Tiles that take it: tensor-core tiles with direct activation loads (swap_ab,
+ * M <= tok_tile, one tile or cluster segment per CTA, at most `stages` k-blocks per CTA;
+ * tile->act 0 or 2), and CUDA-core tiles (split 5; the kernel quantises the batch in its
+ * prologue, 16-byte aligned rows with strides a multiple of 8 elements); any other
+ * returns I8L_ENOTSUP and the caller quantises separately.
  *
  * Replaces the reference's o_proj input path, vLLM's scaled_int8_quant followed by
  * w8a8_mm (bench/fuse_quant.py:234, int8_linear/vllm_fuse_patch.py:13-14, where the
@@ -133,6 +135,44 @@ int i8l_w8a8_mm_quant_act(const void *X, int32_t x_dtype, int64_t ldx, int32_t p
                           void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
                           int32_t K, const i8l_tile *tile, void *workspace,
                           size_t ws_bytes, void *stream);
+
+/*
+ * add + RMSNorm + per-token quantisation of X followed by the GEMM with its result, in
+ * one launch for decode batches of at most 8 tokens: the same bits as
+ * i8l_add_rmsnorm_quant(x, residual, norm_weight) and then i8l_w8a8_mm(q, W, scale, sb),
+ * without the int8 activation or its scales ever reaching HBM.  Every CTA of the
+ * CUDA-core GEMM (split 5) normalises and quantises the whole batch itself, with the
+ * standalone kernel's thread layout and reduction order, before its dot products; CTA 0
+ * writes residual_out = x + residual (rounded to act_dtype), as the standalone kernel
+ * does.  x, residual, residual_out: act_dtype (I8L_BF16/I8L_F16) rows of K values,
+ * 16-byte aligned, row strides multiples of 8; residual and residual_out NULL together
+ * for a plain RMSNorm.  Other arguments as i8l_w8a8_mm (there is no sa: the per-token
+ * scales are the quantiser's).  tile: NULL or zeroed for the CUDA-core tile holding M,
+ * else a split-5 tile; I8L_ENOTSUP for larger batches, other tiles, unaligned rows or a
+ * K whose rows hold more than 8 vectors per thread at this batch (the caller then runs
+ * the two steps).
+ * Replaces the reference's decoder-layer pair add_rmsnorm_quant -> int8 linear
+ * (int8_linear/vllm_fuse_patch.py:41-52, bench/fuse_quant.py:230-236).
+ */
+int i8l_rmsnorm_w8a8_mm(const void *x, int64_t ldx, const void *residual, int64_t ldr,
+                        const void *norm_weight, int32_t act_dtype, int32_t w_dtype, float eps,
+                        int32_t precise_div, void *residual_out, int64_t ldro, const int8_t *W,
+                        int64_t ldw, const float *sb, int32_t sb_per_col, const void *bias,
+                        int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldc, int32_t M,
+                        int32_t N, int32_t K, const i8l_tile *tile, void *stream);
+
+/*
+ * SiLU-and-mul + per-token quantisation of gate_up = [gate | up] (rows of 2K values,
+ * ld elements apart) followed by the GEMM with the [M, K] result, in one launch: the same
+ * bits as i8l_silu_mul_quant and then i8l_w8a8_mm.  Same tile rules as
+ * i8l_rmsnorm_w8a8_mm.  Replaces the reference's MLP pair silu_mul_quant -> down_proj
+ * (int8_linear/vllm_fuse_patch.py:55-59, bench/fuse_quant.py:237-238).
+ */
+int i8l_silu_mul_w8a8_mm(const void *gate_up, int64_t ld, int32_t act_dtype, int32_t precise_div,
+                         int32_t round_silu, const int8_t *W, int64_t ldw, const float *sb,
+                         int32_t sb_per_col, const void *bias, int32_t bias_dtype, void *out,
+                         int32_t out_dtype, int64_t ldc, int32_t M, int32_t N, int32_t K,
+                         const i8l_tile *tile, void *stream);
 
 /*
  * i8l_w8a8_mm for callers that cannot allocate device memory.  No counterpart in

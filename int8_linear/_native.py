@@ -54,6 +54,11 @@ SIGNATURES = {
                            _i32, _i32, _i32, ctypes.POINTER(I8LTile), _vp, _sz, _vp]),
     "i8l_w8a8_mm_quant_act": (_i32, [_vp, _i32, _i64, _i32, _i8p, _i64, _fp, _i32, _vp, _i32, _vp, _i32,
                                      _i64, _i32, _i32, _i32, ctypes.POINTER(I8LTile), _vp, _sz, _vp]),
+    "i8l_rmsnorm_w8a8_mm": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i32, _f32, _i32, _vp, _i64, _i8p, _i64,
+                                   _fp, _i32, _vp, _i32, _vp, _i32, _i64, _i32, _i32, _i32,
+                                   ctypes.POINTER(I8LTile), _vp]),
+    "i8l_silu_mul_w8a8_mm": (_i32, [_vp, _i64, _i32, _i32, _i32, _i8p, _i64, _fp, _i32, _vp, _i32, _vp, _i32,
+                                    _i64, _i32, _i32, _i32, ctypes.POINTER(I8LTile), _vp]),
     "i8l_w8a8_mm_noalloc": (_i32, [_i8p, _i64, _i8p, _i64, _fp, _i32, _fp, _i32, _vp, _i32, _vp, _i32,
                                    _i64, _i32, _i32, _i32, ctypes.POINTER(I8LTile), _vp]),
     "i8l_workspace_size": (_sz, [_i32, _i32, _i32, ctypes.POINTER(I8LTile)]),

@@ -1617,9 +1617,13 @@ static int gemm_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, 
       return set_error(I8L_ENOTSUP, "bias dtype code %d not supported", bias_dtype);
   }
   if (tile && tile->split == 5) {
-    if (aq)
-      return set_error(I8L_ENOTSUP, "fused activation quantisation needs direct activation loads, "
-                                    "which CUDA-core tiles (split 5) do not have");
+    if (aq) {
+      // CUDA-core tile: the kernel's prologue quantises the activation per token.
+      const GemvPro pro{1, aq->x, aq->ldx, aq->dtype, nullptr, 0, nullptr, 0, nullptr, 0, 0.f,
+                        aq->precise, 0};
+      return gemv_run(nullptr, 0, W, ldw, nullptr, 0, sb, sb_per_col, bias, bias_dtype, out, out_dtype,
+                      ldc, M, N, K, tile, stream, &pro);
+    }
     return gemv_run(A, lda, W, ldw, sa, sa_per_row, sb, sb_per_col, bias, bias_dtype, out, out_dtype,
                     ldc, M, N, K, tile, stream);
   }

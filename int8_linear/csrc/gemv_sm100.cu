@@ -31,6 +31,7 @@
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "internal.h"
+#include "rows.cuh"
 
 namespace i8l {
 
@@ -57,6 +58,24 @@ struct GemvArgs {
   int stages;      // ring depth
   int max_rows;    // most rows one CTA owns (sizes the accumulators)
   int *status;
+  // Activation prologue (pro != 0): every CTA makes the int8 activation and its per-token
+  // scales itself from a bf16/fp16 input, as the standalone quantiser kernel would, instead
+  // of reading them: 1 per-token quantisation of X, 2 add + RMSNorm + quantisation of X
+  // (+ residual; CTA 0 writes the residual output), 3 SiLU-and-mul + quantisation of
+  // X = [gate | up].
+  int pro;
+  const void *x;
+  long long ldx;
+  int x_dtype;
+  const void *res;
+  long long ldr;
+  void *rout;
+  long long ldro;
+  const void *nw;
+  int nw_dtype;
+  float eps;
+  int precise, round_silu;
+  int pro_threads;  // threads per row of the standalone kernel (its reduction order)
 };
 
 // Shared memory: barriers | accumulators [max_rows][MT] int32 | activation [M][K] |
@@ -128,10 +147,194 @@ __device__ __forceinline__ int warp_sum_transposed(int (&v)[V], int lane) {
   return r;
 }
 
+// ---------------------------------------------------------------- activation prologue
+__device__ __forceinline__ float half_bits_to_f32(uint32_t h, bool f16) {
+  return f16 ? __half2float(__ushort_as_half(static_cast<unsigned short>(h))) : __uint_as_float(h << 16);
+}
+
+__device__ __forceinline__ void unpack8(const uint4 &r, bool f16, float (&o)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    o[2 * j] = half_bits_to_f32(w[j] & 0xffffu, f16);
+    o[2 * j + 1] = half_bits_to_f32(w[j] >> 16, f16);
+  }
+}
+
+__device__ __forceinline__ uint32_t f32_to_half_bits(float v, bool f16) {
+  if (f16) return __half_as_ushort(__float2half_rn(v));
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float round_act(float v, bool f16) {
+  return f16 ? round_through<I8L_F16>(v) : round_through<I8L_BF16>(v);
+}
+
+__device__ __forceinline__ float round_weight_dtype(float v, int dtype) {
+  return dtype == I8L_BF16 ? round_through<I8L_BF16>(v)
+                           : (dtype == I8L_F16 ? round_through<I8L_F16>(v) : v);
+}
+
+__device__ __forceinline__ float weight_at(const void *w, int dtype, int i) {
+  return dtype == I8L_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(w)[i])
+                           : (dtype == I8L_F16 ? __half2float(static_cast<const __half *>(w)[i])
+                                               : static_cast<const float *>(w)[i]);
+}
+
+// Sums (or maxima) of MT per-row values over the consumer threads, each row in exactly
+// the steps of the standalone kernels' block reduction over `nw` warps: a butterfly in
+// the warp, the warp results in shared memory, then every warp reads them (lanes past nw
+// read 0) and butterflies again.  All MT rows share the two barriers.
+template <int MT, bool kMax>
+__device__ __forceinline__ void rows_reduce(float (&v)[MT], float (*red)[8], int ctid, int nw) {
+  const int lane = ctid & 31, w = ctid >> 5;
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, v[m], o);
+      v[m] = kMax ? fmaxf(v[m], t) : __fadd_rn(v[m], t);
+    }
+  if (lane == 0)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) red[m][w] = v[m];
+  named_bar_sync(1, kGemvConsumers);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    v[m] = lane < nw ? red[m][lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, v[m], o);
+      v[m] = kMax ? fmaxf(v[m], t) : __fadd_rn(v[m], t);
+    }
+  }
+  named_bar_sync(1, kGemvConsumers);
+}
+
+// The M x K int8 activation (into `act`, rows K bytes apart) and its per-token scales
+// (into scale_s) from the prologue's input, with the standalone kernels' arithmetic:
+//   pro 1  quant_rows_kernel        y = x
+//   pro 2  add_rmsnorm_quant_kernel x += res (stored rounded as the residual output);
+//          var = sum(x^2)/K (same per-thread order and reduction tree), xn = x*rsqrt(var+eps),
+//          y = act(weight_dtype(xn) * w)
+//   pro 3  silu_mul_quant_kernel    y = act(act?(g / (1 + exp(-g))) * u)
+// then the row quantiser: scale = absmax/127, q = rint(y * 127/absmax) saturated.  Thread
+// ctid < pro_threads owns vectors (v * pro_threads + ctid) * 8 of every row, as the
+// standalone kernel's thread ctid does.  NVP: vectors per thread.
+template <int MT, int NVP>
+__device__ __forceinline__ void gemv_prologue(const GemvArgs &a, int8_t *act, float *scale_s,
+                                              float (*red)[8], int ctid) {
+  const int K = a.K, th = a.pro_threads, nw = th >> 5;
+  const bool f16 = a.x_dtype == I8L_F16;
+  const auto *xb = static_cast<const uint8_t *>(a.x);
+  float y[MT][NVP][8];
+  float ss[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    ss[m] = 0.f;
+#pragma unroll
+    for (int v = 0; v < NVP; ++v) {
+      const int col = (v * th + ctid) * 8;
+      const bool live = m < a.M && ctid < th && col < K;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[m][v][i] = 0.f;
+      if (!live) continue;
+      const uint4 xr = __ldcg(reinterpret_cast<const uint4 *>(xb + (m * a.ldx + col) * 2));
+      if (a.pro == 3) {
+        const uint4 ur = __ldcg(reinterpret_cast<const uint4 *>(xb + (m * a.ldx + K + col) * 2));
+        float g[8], u[8];
+        unpack8(xr, f16, g);
+        unpack8(ur, f16, u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float sl = div_full(g[i], __fadd_rn(1.0f, expf(-g[i])));
+          if (a.round_silu) sl = round_act(sl, f16);
+          y[m][v][i] = round_act(__fmul_rn(sl, u[i]), f16);
+        }
+      } else {
+        unpack8(xr, f16, y[m][v]);
+        if (a.pro == 2 && a.res) {
+          const uint4 rr = __ldcg(reinterpret_cast<const uint4 *>(
+              static_cast<const uint8_t *>(a.res) + (m * a.ldr + col) * 2));
+          float r[8];
+          unpack8(rr, f16, r);
+          uint32_t packed[4];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[m][v][i] = __fadd_rn(y[m][v][i], r[i]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            packed[j] = f32_to_half_bits(y[m][v][2 * j], f16) | (f32_to_half_bits(y[m][v][2 * j + 1], f16) << 16);
+          if (blockIdx.x == 0)
+            *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(a.rout) + (m * a.ldro + col) * 2) =
+                make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
+        if (a.pro == 2)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ss[m] = __fadd_rn(ss[m], __fmul_rn(y[m][v][i], y[m][v][i]));
+      }
+    }
+  }
+  if (a.pro == 2) {
+    rows_reduce<MT, false>(ss, red, ctid, nw);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float var = div_full(ss[m], static_cast<float>(K));
+      const float rs = rsqrtf(__fadd_rn(var, a.eps));
+#pragma unroll
+      for (int v = 0; v < NVP; ++v) {
+        const int col = (v * th + ctid) * 8;
+        if (!(m < a.M && ctid < th && col < K)) continue;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xn = round_weight_dtype(__fmul_rn(y[m][v][i], rs), a.nw_dtype);
+          y[m][v][i] = round_act(__fmul_rn(xn, weight_at(a.nw, a.nw_dtype, col + i)), f16);
+        }
+      }
+    }
+  }
+  float mx[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    mx[m] = 0.f;
+#pragma unroll
+    for (int v = 0; v < NVP; ++v)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[m] = fmaxf(mx[m], fabsf(y[m][v][i]));
+  }
+  rows_reduce<MT, true>(mx, red, ctid, nw);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    if (m >= a.M) continue;
+    const float amax = mx[m];
+    if (ctid == 0) scale_s[m] = a.precise ? div_rn(amax, 127.f) : div_full(amax, 127.f);
+    const float inv = amax == 0.f ? 0.f : (a.precise ? div_rn(127.f, amax) : div_full(127.f, amax));
+#pragma unroll
+    for (int v = 0; v < NVP; ++v) {
+      const int col = (v * th + ctid) * 8;
+      if (!(ctid < th && col < K)) continue;
+      uint32_t w[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r0 = __float2int_rn(__fmul_rn(y[m][v][4 * h], inv));
+        const int r1 = __float2int_rn(__fmul_rn(y[m][v][4 * h + 1], inv));
+        const int r2 = __float2int_rn(__fmul_rn(y[m][v][4 * h + 2], inv));
+        const int r3 = __float2int_rn(__fmul_rn(y[m][v][4 * h + 3], inv));
+        uint32_t t;
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(t) : "r"(r3), "r"(r2));
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w[h]) : "r"(r1), "r"(r0), "r"(t));
+      }
+      *reinterpret_cast<uint2 *>(act + static_cast<size_t>(m) * K + col) = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
 // MT: most tokens (1, 2, 4 or 8); RG: weight rows per task (activation reuse).
-template <int MT, int RG>
+// NVP: vectors per thread of the activation prologue, 0 for an int8 activation.
+template <int MT, int RG, int NVP>
 __global__ void __launch_bounds__(kGemvThreads, 2) w8a8_gemv_sm100(const GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float pro_red[8][8];
+  __shared__ float pro_scale[8];
   const GemvLayout L(a.stages, a.max_rows, MT, a.M, a.K, a.stage_rows);
   const int S = a.stages;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -199,7 +402,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) w8a8_gemv_sm100(const GemvArg
   const int ctid = threadIdx.x - 32;
   const int cw = warp - 1;
   pdl_wait();  // the activation, scales and output belong to the stream's order
-  {
+  for (int i = ctid; i < rows * MT; i += kGemvConsumers) acc[i] = 0;
+  if constexpr (NVP > 0) {
+    gemv_prologue<MT, NVP>(a, act, pro_scale, pro_red, ctid);
+  } else {
     const int chunks = K / 16;
     const int n = a.M * chunks;
     for (int i = ctid; i < n; i += kGemvConsumers) {
@@ -207,7 +413,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) w8a8_gemv_sm100(const GemvArg
       *reinterpret_cast<uint4 *>(act + static_cast<size_t>(m) * K + c * 16) =
           ld_cg_v4(a.A + m * a.lda + c * 16);
     }
-    for (int i = ctid; i < rows * MT; i += kGemvConsumers) acc[i] = 0;
   }
   named_bar_sync(1, kGemvConsumers);
 
@@ -264,7 +469,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) w8a8_gemv_sm100(const GemvArg
     const int v = acc[r * MT + m];
     float f = 0.f;
     if (!raw) {
-      const float sa = a.sa_per_row ? a.sa[m] : a.sa[0];
+      const float sa = NVP > 0 ? pro_scale[m] : (a.sa_per_row ? a.sa[m] : a.sa[0]);
       const float sb = a.sb_per_col ? a.sb[n] : a.sb[0];
       f = dequant(v, sa, sb, has_bias ? load_scalar_f(a.bias, a.bias_dtype, n) : 0.f, has_bias);
     }
@@ -272,19 +477,19 @@ __global__ void __launch_bounds__(kGemvThreads, 2) w8a8_gemv_sm100(const GemvArg
   }
 }
 
-template <int MT, int RG>
+template <int MT, int RG, int NVP>
 static int launch_gemv(const GemvArgs &a, int ctas, size_t smem, cudaStream_t stream) {
   static size_t configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64 || smem > configured[dev]) {
-    e = cudaFuncSetAttribute(w8a8_gemv_sm100<MT, RG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(w8a8_gemv_sm100<MT, RG, NVP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemv smem)");
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
-  e = launch(w8a8_gemv_sm100<MT, RG>, dim3(ctas), dim3(kGemvThreads), smem, stream, 1, a);
+  e = launch(w8a8_gemv_sm100<MT, RG, NVP>, dim3(ctas), dim3(kGemvThreads), smem, stream, 1, a);
   if (e != cudaSuccess) return cuda_error(e, "gemv launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "gemv launch");
@@ -336,11 +541,55 @@ int gemv_plan(int M, int N, int K, const i8l_tile *t, GemvPlan *p) {
 int gemv_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, const float *sa,
              int32_t sa_per_row, const float *sb, int32_t sb_per_col, const void *bias,
              int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
-             int32_t K, const i8l_tile *tile, void *stream) {
+             int32_t K, const i8l_tile *tile, void *stream, const GemvPro *pro) {
   GemvPlan p;
   int e = gemv_plan(M, N, K, tile, &p);
   if (e) return e;
   GemvArgs a{};
+  int nvp = 0;
+  if (pro) {
+    if (pro->x_dtype != I8L_BF16 && pro->x_dtype != I8L_F16)
+      return set_error(I8L_ENOTSUP, "activation dtype code %d not supported (bf16 or fp16)", pro->x_dtype);
+    if (!pro->x) return set_error(I8L_EINVAL, "NULL activation pointer");
+    if (pro->ldx < (pro->mode == 3 ? 2LL * K : static_cast<long long>(K)))
+      return set_error(I8L_EINVAL, "activation row stride %lld too small for K=%d",
+                       static_cast<long long>(pro->ldx), K);
+    if (K % 8 || pro->ldx % 8 || !aligned16(pro->x))
+      return set_error(I8L_ENOTSUP, "the fused quantiser needs 16-byte aligned activation rows");
+    if (pro->mode == 2) {
+      if (!pro->nw) return set_error(I8L_EINVAL, "NULL norm weight");
+      if (pro->nw_dtype < I8L_BF16 || pro->nw_dtype > I8L_F32)
+        return set_error(I8L_ENOTSUP, "norm weight dtype code %d not supported", pro->nw_dtype);
+      if ((pro->res == nullptr) != (pro->rout == nullptr))
+        return set_error(I8L_EINVAL, "residual and residual_out must be given together");
+      if (pro->res) {
+        if (pro->ldr < K || pro->ldro < K) return set_error(I8L_EINVAL, "residual row stride smaller than K");
+        if (pro->ldr % 8 || pro->ldro % 8 || !aligned16(pro->res) || !aligned16(pro->rout))
+          return set_error(I8L_ENOTSUP, "the fused norm needs 16-byte aligned residual rows");
+      }
+    }
+    RowShape rs;
+    if (!row_shape(K, 8, &rs)) return set_error(I8L_ENOTSUP, "row of %d values is too long", K);
+    nvp = rs.nv;
+    if (rs.threads > kGemvConsumers || nvp > 3 || p.mt * nvp > 8)
+      return set_error(I8L_ENOTSUP,
+                       "the fused quantiser holds at most 8 row vectors of 8 values per thread "
+                       "(%d tokens x %d vectors for K=%d)", p.mt, nvp, K);
+    a.pro = pro->mode;
+    a.x = pro->x;
+    a.ldx = pro->ldx;
+    a.x_dtype = pro->x_dtype;
+    a.res = pro->res;
+    a.ldr = pro->ldr;
+    a.rout = pro->rout;
+    a.ldro = pro->ldro;
+    a.nw = pro->nw;
+    a.nw_dtype = pro->nw_dtype;
+    a.eps = pro->eps;
+    a.precise = pro->precise ? 1 : 0;
+    a.round_silu = pro->round_silu ? 1 : 0;
+    a.pro_threads = rs.threads;
+  }
   a.M = M;
   a.N = N;
   a.K = K;
@@ -362,16 +611,100 @@ int gemv_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, const f
   a.max_rows = p.max_rows;
   a.status = status_ptr();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define I8L_GEMV(MT, RG)                                                      \
+  switch (nvp) {                                                              \
+    case 0: return launch_gemv<MT, RG, 0>(a, p.ctas, p.smem, s);              \
+    case 1: return launch_gemv<MT, RG, (MT <= 8 ? 1 : 0)>(a, p.ctas, p.smem, s); \
+    case 2: return launch_gemv<MT, RG, (MT <= 4 ? 2 : 0)>(a, p.ctas, p.smem, s); \
+    default: return launch_gemv<MT, RG, (MT <= 2 ? 3 : 0)>(a, p.ctas, p.smem, s); \
+  }
   switch (p.mt) {
     case 1:
-      return launch_gemv<1, 8>(a, p.ctas, p.smem, s);
+      I8L_GEMV(1, 8)
     case 2:
-      return launch_gemv<2, 8>(a, p.ctas, p.smem, s);
+      I8L_GEMV(2, 8)
     case 4:
-      return launch_gemv<4, 8>(a, p.ctas, p.smem, s);
+      I8L_GEMV(4, 8)
     default:
-      return launch_gemv<8, 4>(a, p.ctas, p.smem, s);
+      I8L_GEMV(8, 4)
   }
+#undef I8L_GEMV
+}
+
+// Arguments every CUDA-core entry point checks before planning.
+static int gemv_check(const int8_t *W, int64_t ldw, const float *sb, const void *bias, int32_t bias_dtype,
+                      void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N, int32_t K) {
+  if (M < 0 || N < 0 || K < 0) return set_error(I8L_EINVAL, "negative size M=%d N=%d K=%d", M, N, K);
+  if (out_dtype < I8L_BF16 || out_dtype > I8L_I32)
+    return set_error(I8L_ENOTSUP, "output dtype code %d not supported", out_dtype);
+  if (K == 0) return set_error(I8L_ENOTSUP, "K=0 is not supported");
+  if (K % 16) return set_error(I8L_ENOTSUP, "K=%d must be a multiple of 16", K);
+  if (!W || !out) return set_error(I8L_EINVAL, "NULL operand pointer");
+  if (ldw < K || ldc < N) return set_error(I8L_EINVAL, "leading dimensions ldw=%lld ldc=%lld too small",
+                                           static_cast<long long>(ldw), static_cast<long long>(ldc));
+  if (reinterpret_cast<uintptr_t>(W) % 16 || ldw % 16)
+    return set_error(I8L_ENOTSUP, "the int8 weight and its row stride must be 16-byte aligned");
+  if (out_dtype != I8L_I32) {
+    if (!sb) return set_error(I8L_EINVAL, "NULL scale pointer");
+    if (bias && (bias_dtype < I8L_BF16 || bias_dtype > I8L_F32))
+      return set_error(I8L_ENOTSUP, "bias dtype code %d not supported", bias_dtype);
+  }
+  return I8L_OK;
+}
+
+// The tile of a fused-quantiser call: the caller's (a CUDA-core tile), or the CUDA-core
+// tile for the fewest tokens that hold M.
+static int gemv_tile(int32_t M, const i8l_tile *tile, i8l_tile *t) {
+  if (tile && (tile->tok_tile || tile->w_tile || tile->split)) {
+    if (tile->split != 5)
+      return set_error(I8L_ENOTSUP, "the fused quantiser runs on CUDA-core tiles (split 5), got split %d",
+                       tile->split);
+    *t = *tile;
+    return I8L_OK;
+  }
+  if (M > 8) return set_error(I8L_ENOTSUP, "the fused quantiser takes batches of at most 8 tokens, got %d", M);
+  *t = i8l_tile{};
+  t->tok_tile = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+  t->split = 5;
+  if (tile) {
+    t->stages = tile->stages;
+    t->ctas = tile->ctas;
+  }
+  return I8L_OK;
 }
 
 }  // namespace i8l
+
+using namespace i8l;
+
+extern "C" int i8l_rmsnorm_w8a8_mm(const void *x, int64_t ldx, const void *residual, int64_t ldr,
+                                   const void *norm_weight, int32_t act_dtype, int32_t w_dtype,
+                                   float eps, int32_t precise_div, void *residual_out, int64_t ldro,
+                                   const int8_t *W, int64_t ldw, const float *sb, int32_t sb_per_col,
+                                   const void *bias, int32_t bias_dtype, void *out, int32_t out_dtype,
+                                   int64_t ldc, int32_t M, int32_t N, int32_t K, const i8l_tile *tile,
+                                   void *stream) {
+  int e = gemv_check(W, ldw, sb, bias, bias_dtype, out, out_dtype, ldc, M, N, K);
+  if (e || M == 0 || N == 0) return e;
+  i8l_tile t;
+  if ((e = gemv_tile(M, tile, &t))) return e;
+  const GemvPro pro{2, x, ldx, act_dtype, residual, ldr, residual_out, ldro, norm_weight, w_dtype, eps,
+                    precise_div, 0};
+  return gemv_run(nullptr, 0, W, ldw, nullptr, 0, sb, sb_per_col, bias, bias_dtype, out, out_dtype, ldc,
+                  M, N, K, &t, stream, &pro);
+}
+
+extern "C" int i8l_silu_mul_w8a8_mm(const void *gate_up, int64_t ld, int32_t act_dtype,
+                                    int32_t precise_div, int32_t round_silu, const int8_t *W,
+                                    int64_t ldw, const float *sb, int32_t sb_per_col, const void *bias,
+                                    int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldc,
+                                    int32_t M, int32_t N, int32_t K, const i8l_tile *tile, void *stream) {
+  int e = gemv_check(W, ldw, sb, bias, bias_dtype, out, out_dtype, ldc, M, N, K);
+  if (e || M == 0 || N == 0) return e;
+  i8l_tile t;
+  if ((e = gemv_tile(M, tile, &t))) return e;
+  const GemvPro pro{3, gate_up, ld, act_dtype, nullptr, 0, nullptr, 0, nullptr, 0, 0.f, precise_div,
+                    round_silu};
+  return gemv_run(nullptr, 0, W, ldw, nullptr, 0, sb, sb_per_col, bias, bias_dtype, out, out_dtype, ldc,
+                  M, N, K, &t, stream, &pro);
+}

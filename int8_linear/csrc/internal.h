@@ -38,11 +38,27 @@ struct GemvPlan {
   int stages;      // ring depth
   size_t smem;     // dynamic shared memory per CTA
 };
+// The activation prologue of a CUDA-core GEMM: the kernel quantises its own bf16/fp16
+// input (mode 1 per-token, 2 add + RMSNorm, 3 SiLU-and-mul) instead of reading int8.
+struct GemvPro {
+  int mode;
+  const void *x;
+  int64_t ldx;  // elements
+  int x_dtype;
+  const void *res;  // mode 2: residual or NULL
+  int64_t ldr;
+  void *rout;       // mode 2: residual output (with res)
+  int64_t ldro;
+  const void *nw;   // mode 2: norm weight [K]
+  int nw_dtype;
+  float eps;
+  int precise, round_silu;
+};
 int gemv_plan(int M, int N, int K, const i8l_tile *tile, GemvPlan *p);
 int gemv_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, const float *sa,
              int32_t sa_per_row, const float *sb, int32_t sb_per_col, const void *bias,
              int32_t bias_dtype, void *out, int32_t out_dtype, int64_t ldc, int32_t M, int32_t N,
-             int32_t K, const i8l_tile *tile, void *stream);
+             int32_t K, const i8l_tile *tile, void *stream, const GemvPro *pro = nullptr);
 
 // Whether kernels are launched with programmatic stream serialisation (PDL).
 bool pdl_enabled();

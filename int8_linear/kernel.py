@@ -38,7 +38,7 @@ GEMV_TOKENS = (1, 2, 4, 8)   # token counts of the CUDA-core tiles (split 5)
 WORKSPACE_BYTES = 32 << 20
 
 __all__ = ["Config", "NotSupported", "default_config", "tuned_config", "choose_config", "w8a8_mm",
-           "w8a8_mm_quant_act"]
+           "w8a8_mm_quant_act", "rmsnorm_w8a8_mm", "silu_mul_w8a8_mm"]
 
 
 @dataclass(frozen=True)
@@ -382,19 +382,25 @@ def _launch(lib, a, wp, ldw, sa, sb, bias, out, raw, out_dtype, m, n, k, tile, w
 
 
 def fused_act_config(cfg: Config) -> Config | None:
-    """The tiling of cfg with direct activation loads (which the fused activation
-    quantisation rides on), or None when cfg is not a swap_ab tile."""
+    """The tiling of cfg that w8a8_mm_quant_act can fuse into: a CUDA-core tile itself, the
+    same swap_ab tiling with direct activation loads, or None for other tiles."""
+    if cfg.split == 5:
+        return cfg
     if not cfg.swapped:
         return None
     return cfg if cfg.act == 2 else replace(cfg, act=2)
 
 
 def _fused_candidates(m: int, n: int, k: int) -> list[Config]:
-    """Tilings w8a8_mm_quant_act tries, in order, when the caller names none: the
-    table's (with direct loads), then cluster split-K tilings of the smallest token tile
-    that holds M, then whole tiles, one per CTA."""
+    """Tilings w8a8_mm_quant_act tries, in order, when the caller names none: the table's
+    CUDA-core tile (its prologue quantises), or the table's tile with direct loads, then
+    cluster split-K tilings of the smallest token tile that holds M, then whole tiles,
+    one per CTA."""
     out = []
-    base = fused_act_config(choose_config(m, n, k))
+    chosen = choose_config(m, n, k)
+    if chosen.split == 5:
+        return [chosen]
+    base = fused_act_config(chosen)
     if base is not None:
         out.append(base)
     if m <= 64:
@@ -505,3 +511,108 @@ def dequant_i32(acc: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
             _DTYPE_CODE[bias.dtype] if bias is not None else 0, out.data_ptr(), _DTYPE_CODE[out_dtype],
             out.stride(0), m, n, torch.cuda.current_stream(acc.device).cuda_stream))
     return out
+
+
+def _gemv_fused_config(m: int, n: int, k: int, config: Config | None) -> Config | None:
+    """The CUDA-core tile a fused-quantiser call runs on, or None to run the two steps:
+    the caller's tiling if it is one, else the library's choice for the shape if it is one."""
+    cfg = config if config is not None else choose_config(m, n, k)
+    return cfg if cfg.split == 5 else None
+
+
+def _gemv_args(b_q, scale_b, bias, out_dtype, n):
+    if b_q.dtype != torch.int8 or b_q.dim() != 2:
+        raise NotSupported("b_q must be a 2-D int8 weight")
+    sb = scale_b if scale_b.is_contiguous() else scale_b.contiguous()
+    if sb.dtype != torch.float32 or sb.numel() not in (1, n):
+        raise ValueError(f"scale_b must hold 1 or {n} float32 values")
+    if bias is not None:
+        if tuple(bias.shape) != (n,):
+            raise ValueError(f"bias must have shape ({n},), got {tuple(bias.shape)}")
+        if bias.dtype not in _DTYPE_CODE:
+            raise NotSupported(f"bias dtype {bias.dtype} not supported")
+        bias = bias.contiguous()
+    if out_dtype not in _DTYPE_CODE:
+        raise NotSupported(f"output dtype {out_dtype} not supported")
+    return sb, bias
+
+
+def rmsnorm_w8a8_mm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor, eps: float,
+                    b_q: torch.Tensor, scale_b: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+                    bias: torch.Tensor | None = None, *, precise_div: bool = True,
+                    config: Config | None = None):
+    """`q, s, rout = add_rmsnorm_quant(x, residual, weight, eps, precise_div)` followed by
+    `w8a8_mm(q, b_q, s, scale_b, out_dtype, bias)`: returns (out, rout), the same bits.
+
+    For decode batches on a CUDA-core tile (the library's choice for M <= 8 on most
+    shapes, or `config`), one kernel does both: every CTA normalises and quantises the
+    batch in its prologue (the standalone kernel's thread layout and reduction order)
+    and the int8 activation never reaches HBM.  Otherwise the two steps run.  This is the
+    reference's decoder-layer pair, add_rmsnorm_quant then the int8 linear
+    (int8_linear/vllm_fuse_patch.py:41-52)."""
+    from int8_linear.fused_quant import _WEIGHT, add_rmsnorm_quant
+
+    m, k = x.shape
+    n = b_q.shape[1]
+    cfg = _gemv_fused_config(m, n, k, config) if x.dim() == 2 and b_q.shape[0] == k else None
+    if cfg is not None and m > 0 and n > 0 and x.dtype in (torch.bfloat16, torch.float16) \
+            and x.is_cuda and x.stride(1) == 1 and weight.dtype in _WEIGHT and weight.numel() == k \
+            and b_q.stride(0) == 1:
+        sb, bias = _gemv_args(b_q, scale_b, bias, out_dtype, n)
+        w = weight.contiguous()
+        rout = None
+        if residual is not None:
+            if residual.shape != x.shape or residual.dtype != x.dtype:
+                raise ValueError("residual must match x in shape and dtype")
+            rout = torch.empty_like(x)
+        out = torch.empty((m, n), dtype=out_dtype, device=x.device)
+        dev = x.get_device()
+        code = _native.load().i8l_rmsnorm_w8a8_mm(
+            x.data_ptr(), x.stride(0),
+            residual.data_ptr() if residual is not None else None,
+            residual.stride(0) if residual is not None else 0,
+            w.data_ptr(), _native.BF16 if x.dtype == torch.bfloat16 else _native.F16, _WEIGHT[w.dtype],
+            float(eps), int(bool(precise_div)), rout.data_ptr() if rout is not None else None,
+            rout.stride(0) if rout is not None else 0, b_q.data_ptr(), b_q.stride(1), sb.data_ptr(),
+            int(sb.numel() > 1), bias.data_ptr() if bias is not None else None,
+            _DTYPE_CODE[bias.dtype] if bias is not None else 0, out.data_ptr(), _DTYPE_CODE[out_dtype],
+            out.stride(0), m, n, k, ctypes.byref(_tile_of(cfg)), current_stream(dev))
+        if code != _native.ENOTSUP:
+            _native.check(code)
+            return out, rout
+    q, s, rout = add_rmsnorm_quant(x.contiguous(), residual, weight, eps, precise_div)
+    return w8a8_mm(q, b_q, s, scale_b, out_dtype, bias, config=config), rout
+
+
+def silu_mul_w8a8_mm(gate_up: torch.Tensor, b_q: torch.Tensor, scale_b: torch.Tensor,
+                     out_dtype: torch.dtype = torch.bfloat16, bias: torch.Tensor | None = None, *,
+                     precise_div: bool = True, round_silu: bool = False,
+                     config: Config | None = None) -> torch.Tensor:
+    """`q, s = silu_mul_quant(gate_up, precise_div, round_silu)` followed by
+    `w8a8_mm(q, b_q, s, scale_b, out_dtype, bias)`, the same bits; one kernel on a
+    CUDA-core tile (SiLU-and-mul and the quantiser in every CTA's prologue), else the two
+    steps.  The reference's MLP pair, silu_mul_quant then down_proj
+    (int8_linear/vllm_fuse_patch.py:55-59)."""
+    from int8_linear.fused_quant import silu_mul_quant
+
+    m, i2 = gate_up.shape
+    k = i2 // 2
+    n = b_q.shape[1]
+    cfg = _gemv_fused_config(m, n, k, config) if b_q.shape[0] == k else None
+    if cfg is not None and m > 0 and n > 0 and gate_up.dtype in (torch.bfloat16, torch.float16) \
+            and gate_up.is_cuda and gate_up.stride(1) == 1 and b_q.stride(0) == 1:
+        sb, bias = _gemv_args(b_q, scale_b, bias, out_dtype, n)
+        out = torch.empty((m, n), dtype=out_dtype, device=gate_up.device)
+        dev = gate_up.get_device()
+        code = _native.load().i8l_silu_mul_w8a8_mm(
+            gate_up.data_ptr(), gate_up.stride(0),
+            _native.BF16 if gate_up.dtype == torch.bfloat16 else _native.F16, int(bool(precise_div)),
+            int(bool(round_silu)), b_q.data_ptr(), b_q.stride(1), sb.data_ptr(), int(sb.numel() > 1),
+            bias.data_ptr() if bias is not None else None, _DTYPE_CODE[bias.dtype] if bias is not None else 0,
+            out.data_ptr(), _DTYPE_CODE[out_dtype], out.stride(0), m, n, k,
+            ctypes.byref(_tile_of(cfg)), current_stream(dev))
+        if code != _native.ENOTSUP:
+            _native.check(code)
+            return out
+    q, s = silu_mul_quant(gate_up.contiguous(), precise_div, round_silu)
+    return w8a8_mm(q, b_q, s, scale_b, out_dtype, bias, config=config)

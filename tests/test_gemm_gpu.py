@@ -341,14 +341,14 @@ def test_out_argument_writes_in_place_with_the_same_bits():
 
 @pytest.mark.parametrize("m", [1, 2])
 @pytest.mark.parametrize("k,n", [(1040, 1000), (1536, 256), (6144, 8192), (2048, 100)])
-def test_untuned_one_and_two_token_batches_take_narrow_tiles_bit_exact(m, k, n):
+def test_untuned_one_and_two_token_batches_take_cuda_core_tiles_bit_exact(m, k, n):
     """Shapes missing from the tuned table fall to default_config, which sends one- and
-    two-token batches on moderate weights to narrow tiles: exact like every tiling."""
+    two-token batches to CUDA-core tiles: exact like every tiling."""
     from int8_linear.kernel import default_config, tuned_config
 
     assert tuned_config(m, n, k) is None
     cfg = default_config(m, n, k)
-    assert cfg.split == 3 and not cfg.swapped
+    assert cfg.split == 5 and cfg.bm >= m
     a, w = ints((m, k), 700 + m), ints((n, k), 701)
     g = torch.Generator().manual_seed(702)
     sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()

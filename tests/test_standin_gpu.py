@@ -62,7 +62,7 @@ def check_norm(ins, outs):
 def test_every_op_of_the_step_matches_the_oracle(m, gamma):
     g = torch.Generator().manual_seed(5)
     w = (torch.ones(HIDDEN) if gamma == "ones" else 1.0 + 0.1 * torch.randn(HIDDEN, generator=g))
-    dec = StandinDecoder(m, layers=3, norm_weight=w.to(torch.bfloat16).cuda())
+    dec = StandinDecoder(m, layers=3, norm_weight=w.to(torch.bfloat16).cuda(), fuse=False)
     rec: list = []
     out = dec.step(record=rec)
     torch.cuda.synchronize()
@@ -113,3 +113,24 @@ def test_every_op_of_the_step_matches_the_oracle(m, gamma):
             check_gemm(ins, outs)
         prev_out[name] = outs
     assert same(out, prev_out["down_proj"])
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 8, 16])
+def test_fused_step_equals_the_step_of_separate_ops(m):
+    """With the quantisers in the GEMM prologues (CUDA-core tiles) the step gives the
+    same bits as the step of separate quantiser and GEMM launches, eagerly and replayed
+    from a CUDA graph; and the fused ops really ran as fused kernels where they can."""
+    g = torch.Generator().manual_seed(6)
+    w = (1.0 + 0.1 * torch.randn(HIDDEN, generator=g)).to(torch.bfloat16).cuda()
+    dec = StandinDecoder(m, layers=3, norm_weight=w, fuse=False)
+    want = dec.step().clone()
+    assert dec.launches_per_step == 1 + 7 * 3 + 2
+    dec.fuse = {"qkv_proj", "o_proj", "gate_up_proj", "down_proj"}
+    assert torch.equal(dec.step(), want)
+    dec.capture().replay()
+    torch.cuda.synchronize()
+    assert torch.equal(dec.out, want)
+    if m <= 2:   # every quantiser fused: 4 launches per layer
+        assert dec.launches_per_step == 4 * 3
+    dec.fuse = True    # the measured per-batch choice
+    assert torch.equal(dec.step(), want)
