@@ -56,7 +56,7 @@ extern "C" {
  *                distributed shared memory (swap_ab tiles of up to 256 tokens, as the
  *                partial sums fit the leader's ring; no workspace); 4 = CTA pairs
  *                (cta_group::2) on 128 x 256 tiles; 5 = CUDA-core tiles for batches of
- *                at most tok_tile in {1, 2, 4, 8} tokens (w_tile 0, swap_ab 0): each CTA
+ *                at most tok_tile in {1, 2, 4, 8, 16} tokens (w_tile 0, swap_ab 0): each CTA
  *                owns whole output columns (dp4a int8 dot products, no split-K, no
  *                workspace), its weight rows streamed into shared memory by 1-D bulk
  *                copies; `ctas` and `stages` apply;

@@ -329,9 +329,11 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs &a, int8_t *act, fl
 }
 
 // MT: most tokens (1, 2, 4 or 8); RG: weight rows per task (activation reuse).
-// NVP: vectors per thread of the activation prologue, 0 for an int8 activation.
+// NVP: vectors per thread of the activation prologue, 0 for an int8 activation.  Up to 8
+// tokens two CTAs share an SM (the next kernel's beside this one); 16 tokens hold more
+// registers (one CTA per SM).
 template <int MT, int RG, int NVP>
-__global__ void __launch_bounds__(kGemvThreads, 2) w8a8_gemv_sm100(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, MT <= 8 ? 2 : 1) w8a8_gemv_sm100(const GemvArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float pro_red[8][8];
   __shared__ float pro_scale[8];
@@ -504,8 +506,8 @@ int gemv_plan(int M, int N, int K, const i8l_tile *t, GemvPlan *p) {
   int e = device_info(&di);
   if (e) return e;
   const int mt = t->tok_tile;
-  if (mt != 1 && mt != 2 && mt != 4 && mt != 8)
-    return set_error(I8L_ENOTSUP, "CUDA-core tiles (split 5) take tok_tile 1, 2, 4 or 8, got %d", mt);
+  if (mt != 1 && mt != 2 && mt != 4 && mt != 8 && mt != 16)
+    return set_error(I8L_ENOTSUP, "CUDA-core tiles (split 5) take tok_tile 1, 2, 4, 8 or 16, got %d", mt);
   if (M > mt)
     return set_error(I8L_ENOTSUP, "CUDA-core tile for %d tokens given M=%d", mt, M);
   p->mt = mt;
@@ -514,7 +516,7 @@ int gemv_plan(int M, int N, int K, const i8l_tile *t, GemvPlan *p) {
   // Stages of about 32 KB of whole rows (bulk copies that size reach the SM's full ingest
   // rate), rounded up to whole row groups of the kernel's tasks when that stays <= 48 KB,
   // at most one CTA's rows.
-  const int rg = mt == 8 ? 4 : 8;
+  const int rg = mt == 16 ? 2 : (mt == 8 ? 4 : 8);
   int sr = std::max(1, 32768 / K);
   const int sr_groups = (sr + rg - 1) / rg * rg;
   if (static_cast<long long>(sr_groups) * K <= 49152) sr = sr_groups;
@@ -524,7 +526,7 @@ int gemv_plan(int M, int N, int K, const i8l_tile *t, GemvPlan *p) {
   const size_t stage = static_cast<size_t>(p->stage_rows) * K;
   // stages = 0: as many as fit beside a second CTA on the SM (the next kernel's, under
   // programmatic dependent launch); a given depth is capped by what one CTA can hold.
-  const long long budget = t->stages > 0 ? di.max_smem_optin : kGemvHalfSmem;
+  const long long budget = (t->stages > 0 || mt == 16) ? di.max_smem_optin : kGemvHalfSmem;
   const long long fit = (budget - static_cast<long long>(fixed)) / static_cast<long long>(stage);
   long long st = t->stages > 0 ? std::min<long long>(t->stages, fit) : fit;
   st = std::max(1LL, std::min<long long>(st, std::max(needed, 1)));
@@ -617,6 +619,10 @@ int gemv_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, const f
     case 1: return launch_gemv<MT, RG, (MT <= 8 ? 1 : 0)>(a, p.ctas, p.smem, s); \
     case 2: return launch_gemv<MT, RG, (MT <= 4 ? 2 : 0)>(a, p.ctas, p.smem, s); \
     default: return launch_gemv<MT, RG, (MT <= 2 ? 3 : 0)>(a, p.ctas, p.smem, s); \
+  }
+  if (p.mt == 16) {
+    if (nvp) return set_error(I8L_ENOTSUP, "the fused quantiser takes batches of at most 8 tokens");
+    return launch_gemv<16, 2, 0>(a, p.ctas, p.smem, s);
   }
   switch (p.mt) {
     case 1:

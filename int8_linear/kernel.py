@@ -31,7 +31,7 @@ from int8_linear._native import NotSupported
 
 TUNED_PATH = Path(__file__).with_name("tuned_configs.json")
 TOKEN_TILES = (16, 32, 64, 128, 256)
-GEMV_TOKENS = (1, 2, 4, 8)   # token counts of the CUDA-core tiles (split 5)
+GEMV_TOKENS = (1, 2, 4, 8, 16)   # token counts of the CUDA-core tiles (split 5)
 # Split-K workspace kept per (device, stream); kernels leave it zero-filled.  The
 # largest plan needs (SMs - 1) slots of 128 x 256 int32 plus counters, ~19 MB on
 # 148 SMs, so one allocation covers every call.
@@ -62,8 +62,8 @@ class Config:
             128 x 256 tiles for batches of <= 16 tokens: the weight on the MMA's N side,
             256 weight rows per MMA instruction), 4 CTA pairs (two SMs
             per 256 x 256 tile with 256-row tcgen05 MMAs; 128 x 256 tiles, no swap_ab),
-            5 CUDA-core tiles for decode batches of at most 8 tokens: bm in (1, 2, 4, 8)
-            is the most tokens, bn = 0; each CTA owns whole output columns (int8 dot
+            5 CUDA-core tiles for decode batches of at most 16 tokens: bm in
+            (1, 2, 4, 8, 16) is the most tokens, bn = 0; each CTA owns whole output columns (int8 dot
             products with dp4a, no split-K), its weight rows streamed into shared memory
             by 1-D bulk copies that start before the dependency wait.
     ctas    persistent CTAs, 0 for one per SM.
@@ -190,7 +190,7 @@ _chosen: dict[tuple[int, int, int, int], Config] = {}
 
 def _fits(cfg: Config, m: int, n: int, k: int) -> Config:
     """cfg adapted to M when a table bucket's tiling cannot hold it: a CUDA-core tile for
-    fewer tokens than M takes the next larger token count (up to 8), else the default."""
+    fewer tokens than M takes the next larger token count (up to 16), else the default."""
     if cfg.split == 5 and m > cfg.bm:
         bigger = [t for t in GEMV_TOKENS if t >= m]
         return replace(cfg, bm=bigger[0]) if bigger else default_config(m, n, k)

@@ -78,7 +78,7 @@ def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
             if m <= 32:   # plain versus TMA stores for the few output rows
                 out += [Config(tn, 128, split=3, cluster=c, store=1) for c in (2, 4)]
                 out += [Config(tn, 128, split=1, store=1), Config(tn, 128, split=2, store=2)]
-    if m <= 8:    # CUDA-core tiles: whole output columns per CTA, no split-K
+    if m <= 16:   # CUDA-core tiles: whole output columns per CTA, no split-K
         mt = next(t for t in GEMV_TOKENS if t >= m)
         out += [Config(mt, 0, split=5), Config(mt, 0, split=5, ctas=2 * sms),
                 Config(mt, 0, split=5, stages=16)]

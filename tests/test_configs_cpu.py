@@ -35,7 +35,8 @@ def test_choose_config_fits_a_cuda_core_bucket_to_the_batch(monkeypatch):
     monkeypatch.setattr(kernel, "_chosen", {})
     assert kernel.choose_config(3, 4096, 2048).bm == 4
     assert kernel.choose_config(5, 4096, 2048) == Config(8, 0, split=5)       # bumped to 8 tokens
-    assert kernel.choose_config(12, 4096, 2048) == default_config(12, 4096, 2048)
+    assert kernel.choose_config(12, 4096, 2048) == Config(16, 0, split=5)      # up to 16 tokens
+    assert kernel.choose_config(20, 4096, 2048) == default_config(20, 4096, 2048)
 
 
 def test_tuned_table_entries_are_valid_tilings():
@@ -105,7 +106,7 @@ def test_cuda_core_tiles_are_valid_configs():
     assert not cfg.swapped and cfg.name == "gemv m4 s0 c100"
     t = cfg.as_tile()
     assert (t.swap_ab, t.tok_tile, t.w_tile, t.split, t.ctas) == (0, 4, 0, 5, 100)
-    for bad in (Config(3, 0, split=5), Config(16, 0, split=5), Config(8, 128, split=5)):
+    for bad in (Config(3, 0, split=5), Config(32, 0, split=5), Config(8, 128, split=5)):
         with pytest.raises(NotSupported):
             bad.check()
     # cluster split-K now takes the wider token tiles too

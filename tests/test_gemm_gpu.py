@@ -364,7 +364,7 @@ GEMV_SHAPES = [(16, 1), (48, 77), (2048, 4096), (6144, 2048), (2048, 12288), (14
                (4096, 28672)]
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13, 16])
 @pytest.mark.parametrize("k,n", GEMV_SHAPES)
 def test_cuda_core_tiles_bit_exact(m, k, n):
     """CUDA-core tiles (split 5): whole output columns per CTA, dp4a dot products; the
@@ -374,7 +374,7 @@ def test_cuda_core_tiles_bit_exact(m, k, n):
     sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
     sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
-    cfg = Config(next(t for t in (1, 2, 4, 8) if t >= m), 0, split=5)
+    cfg = Config(next(t for t in (1, 2, 4, 8, 16) if t >= m), 0, split=5)
     want = exact(a, w)
     assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), want)
     for dt, code in ((torch.bfloat16, "bf16"), (torch.float16, "f16"), (torch.float32, "f32")):
@@ -384,7 +384,8 @@ def test_cuda_core_tiles_bit_exact(m, k, n):
 
 @pytest.mark.parametrize("cfg", [Config(8, 0, split=5, ctas=1), Config(4, 0, split=5, ctas=7),
                                  Config(8, 0, split=5, ctas=300), Config(2, 0, split=5, stages=1),
-                                 Config(4, 0, split=5, stages=2), Config(8, 0, split=5, stages=3, ctas=37)],
+                                 Config(4, 0, split=5, stages=2), Config(8, 0, split=5, stages=3, ctas=37),
+                                 Config(16, 0, split=5), Config(16, 0, split=5, ctas=296, stages=2)],
                          ids=lambda c: c.name)
 def test_cuda_core_tiles_under_other_grids(cfg):
     """Fewer and more CTAs than SMs (each owning a contiguous column range) and short rings
@@ -413,6 +414,8 @@ def test_cuda_core_tiles_on_strided_operands():
 def test_cuda_core_tiles_decline_larger_batches():
     with pytest.raises(NotSupported):
         w8a8_mm(ints((9, 2048), 1), ints((64, 2048), 2).t(), one(), one(), config=Config(8, 0, split=5))
+    with pytest.raises(NotSupported):
+        w8a8_mm(ints((17, 2048), 1), ints((64, 2048), 2).t(), one(), one(), config=Config(16, 0, split=5))
 
 
 @pytest.mark.parametrize("m", [65, 100, 128, 200, 256])

@@ -8,6 +8,7 @@ equal the one-process result bit for bit, as it does on GPUs with the CUDA kerne
 
 from __future__ import annotations
 
+import io
 import os
 import tempfile
 
@@ -95,7 +96,11 @@ def _worker(rank, path, q):
         gu_shard = torch.cat([tp.shard_cols_of(gu[:, :k], rank, WORLD),
                               tp.shard_cols_of(gu[:, k:], rank, WORLD)], dim=1)
         res["silu"] = tp.sharded_silu_mul_quant(gu_shard, ops=ops)
-        q.put((rank, res))
+        # by value: tensors on a queue travel as shared-memory file descriptors, which
+        # the parent cannot open once this process has exited
+        buf = io.BytesIO()
+        torch.save(res, buf)
+        q.put((rank, buf.getvalue()))
     finally:
         dist.destroy_process_group()
 
@@ -122,8 +127,8 @@ def results():
     deadline = time.time() + 180
     while len(out) < WORLD and time.time() < deadline:
         try:
-            r, res = q.get(timeout=1)
-            out[r] = res
+            r, blob = q.get(timeout=1)
+            out[r] = torch.load(io.BytesIO(blob))
         except _queue.Empty:
             if any(p.exitcode not in (None, 0) for p in procs):
                 break
