@@ -376,6 +376,10 @@ def test_cuda_core_tiles_bit_exact(m, k, n):
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
     cfg = Config(next(t for t in (1, 2, 4, 8, 16) if t >= m), 0, split=5)
     want = exact(a, w)
+    if m * k > 200_000:   # the M x K activation and one ring stage exceed shared memory
+        with pytest.raises(NotSupported, match="shared memory"):
+            w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
+        return
     assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), want)
     for dt, code in ((torch.bfloat16, "bf16"), (torch.float16, "f16"), (torch.float32, "f32")):
         got = w8a8_mm(a, w.t(), sa, sb, dt, bias, config=cfg)
