@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-triton]
                     [--model qwen3-1.7b-vllm|llama-3-8b] [--no-standin] [--no-e2e] [--no-pdl]
                     [--out FILE] [--detail FILE]
-    python bench.py --case gemm|sweep|quant|standin [--shape ...] [...]   (profiling workloads)
+    python bench.py --case gemm|sweep|quant|dequant|standin [--shape ...] [...]   (profiling workloads)
 
 Workload: the per-layer sweep at the Qwen3-1.7B shapes vLLM runs
 (qkv 2048x4096, o_proj 2048x2048, gate_up 2048x12288, down 6144x2048), every M in
@@ -94,7 +94,7 @@ def parse():
     ap.add_argument("--out", default=None, help="also write the final JSON line to this file")
     ap.add_argument("--detail", default=None, help="where the per-shape tables go")
     # profiling workloads (small, self-contained; for ncu captures)
-    ap.add_argument("--case", choices=["gemm", "sweep", "quant", "standin"], default=None)
+    ap.add_argument("--case", choices=["gemm", "sweep", "quant", "dequant", "standin"], default=None)
     ap.add_argument("--shape", default=None, help="gemm: M,N,K; quant: M; standin: batch")
     ap.add_argument("--config", default=None, help="gemm: bm,bn[,split[,cluster]]")
     ap.add_argument("--kind", default="norm", choices=["norm", "silu", "plain"])
@@ -1057,6 +1057,7 @@ def run_case(args) -> None:
         --case gemm --shape M,N,K [--config bm,bn[,split[,cluster]]]   one GEMM, 2 weights
         --case sweep [--model M]                                      every (layer, M) once
         --case quant --shape M --kind norm|silu|plain                 one quantiser
+        --case dequant --shape M,N                                    int32 product -> bf16
         --case standin --shape B                                      stand-in step replays
     """
     import torch
@@ -1103,6 +1104,15 @@ def run_case(args) -> None:
                 fq.silu_mul_quant(gu, True, True)
             else:
                 fq.per_token_quant(x)
+    elif args.case == "dequant":
+        from int8_linear.kernel import dequant_i32
+
+        m, n = (int(v) for v in args.shape.split(","))
+        acc = torch.randint(-(1 << 20), 1 << 20, (m, n), dtype=torch.int32, device="cuda", generator=g)
+        sa = torch.rand((m, 1), device="cuda", generator=g) * 1e-2 + 1e-3
+        sb = torch.rand((n, 1), device="cuda", generator=g) * 1e-3 + 1e-4
+        for _ in range(args.iters):
+            dequant_i32(acc, sa, sb, torch.bfloat16)
     else:
         from int8_linear.standin import StandinDecoder
 
