@@ -1054,7 +1054,7 @@ def run_case(args) -> None:
     a few launches (`--iters`) after the first, so `ncu -s <skip> -c <count>` can pick
     steady-state launches, and keeps the device footprint small.
 
-        --case gemm --shape M,N,K [--config bm,bn[,split[,cluster]]]   one GEMM, 2 weights
+        --case gemm --shape M,N,K [--config bm,bn[,split[,cluster[,swap]]]]   one GEMM, 2 weights
         --case sweep [--model M]                                      every (layer, M) once
         --case quant --shape M --kind norm|silu|plain                 one quantiser
         --case dequant --shape M,N                                    int32 product -> bf16
@@ -1077,7 +1077,8 @@ def run_case(args) -> None:
         cfg = None
         if args.config:
             f = [int(v) for v in args.config.split(",")]
-            cfg = Config(f[0], f[1], split=f[2] if len(f) > 2 else 0, cluster=f[3] if len(f) > 3 else 0)
+            cfg = Config(f[0], f[1], split=f[2] if len(f) > 2 else 0, cluster=f[3] if len(f) > 3 else 0,
+                         swap_ab=bool(f[4]) if len(f) > 4 else None)
         a, ws = ints((m, k)), [ints((n, k)) for _ in range(2)]
         sa = torch.rand((m, 1), device="cuda", generator=g) * 1e-2 + 1e-3
         sb = torch.rand((n, 1), device="cuda", generator=g) * 1e-3 + 1e-4

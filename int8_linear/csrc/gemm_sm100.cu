@@ -65,7 +65,10 @@ struct GemmArgs {
   int *counters;  // one k-block counter per slot
   int *status;
   int cluster;    // >1: the CTAs of each cluster split K of one tile (reduced over DSMEM)
-  int cluster_early;  // contributors push into the leader's staging area without waiting
+  // Partial sums are received in the staging area (free from the start with plain
+  // stores), so senders push as soon as their own MMAs are done; else in the
+  // receiver's operand ring once its MMAs are done and it has said so.
+  int cluster_early;
   // Direct activation loads (swap tiles holding every token, one segment per CTA whose
   // k-blocks all fit in the ring): the epilogue warps copy A's k-blocks into the ring's
   // Y slots with plain loads after the dependency wait, so the activation never queues
@@ -629,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
   uint64_t *acc_empty = acc_full + 2;
   uint64_t *drain = acc_empty + 2;
   uint64_t *peer_bar = drain + 1;  // cluster leader: contributors' partial sums have landed
-  uint64_t *done_bar = drain + 2;  // cluster contributor: the leader's ring is free for them
+  uint64_t *done_bar = drain + 2;  // cluster sender: the receivers' rings are free for it
   uint64_t *act_bar = drain + 3;   // direct activation loads have landed in the Y slots
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -649,17 +652,30 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
     }
     mbar_init(drain, 1);
     mbar_init(peer_bar, 1);
-    mbar_init(done_bar, 1);
+    // Narrow tiles: the leader's go; swap_ab tiles: one arrival from each other CTA.
+    mbar_init(done_bar, (!kNarrow && !kPair && a.cluster > 1) ? a.cluster - 1 : 1);
     mbar_init(act_bar, kEpiWarps);
-    if (a.cluster_early && cluster_ctarank() == 0) {
+    if (kNarrow && a.cluster_early && cluster_ctarank() == 0) {
       // One tile per cluster: its partial sums arrive as (cluster-1) slots of the
-      // live column chunks (narrow tiles: of the M token rows only).  Armed before the
-      // cluster sync, so before any byte lands.
+      // live column chunks of the M token rows.  Armed before the cluster sync, so
+      // before any byte lands.
       int tx, ty;
       tile_coords(a, static_cast<int>(blockIdx.x) / a.cluster, tx, ty);
       const int nch = (live_cols<TN>(a, ty) + 15) / 16;
-      const int rows = kNarrow ? a.M : kXRows;
-      mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * rows * 4));
+      mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * a.M * 4));
+    }
+    if constexpr (!kNarrow && !kPair) {
+      if (a.cluster > 1) {
+        // Spread reduction (swap_ab tiles): 16-column chunk c of the tile belongs to CTA
+        // rank c % cluster, which receives it from the other (cluster-1) CTAs.  Armed
+        // before the cluster sync, so before any byte lands.
+        int tx, ty;
+        tile_coords(a, static_cast<int>(blockIdx.x) / a.cluster, tx, ty);
+        const int nch = (live_cols<TN>(a, ty) + 15) / 16;
+        const int r = static_cast<int>(cluster_ctarank());
+        const int owned = nch > r ? (nch - r + a.cluster - 1) / a.cluster : 0;
+        mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * owned * 16 * kXRows * 4));
+      }
     }
     *abort_flag = 0;
     *last_flag = 0;
@@ -1053,72 +1069,72 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
           }
         }
       } else if (a.cluster > 1) {
-        // Cluster split-K.  Once a CTA's MMAs are done its operand ring is idle.  The
-        // leader (rank 0) then arms its receive barrier and tells each contributor to
-        // go; contributors push their int32 partial sums into slot rank-1 of the
-        // leader's ring ([128 rows][TN] each) with st.async, which completes the
-        // barrier by bytes; the leader adds the slots to its own accumulator.
-        // Early mode: the slots are the leader's staging area, free from the start (the
-        // leader then stores directly), so contributors push as soon as they are done.
-        uint32_t *ring = reinterpret_cast<uint32_t *>(a.cluster_early ? staging : sx);
+        // Cluster split-K, spread reduction.  Each CTA holds the partial sums of its k
+        // range for the whole tile; 16-column chunk c is finished by CTA rank
+        // c % cluster.  Every CTA pushes the chunks it does not own into slot
+        // (sender) of the owner's receive area with st.async, which completes the
+        // owner's barrier by bytes, then adds the (cluster-1) received slots to its own
+        // chunks, dequantises and stores them.  Each SM thus takes in (cluster-1)/cluster
+        // of one tile's partial sums and stores 1/cluster of the tile, where a single
+        // leader would take in (cluster-1) tiles' worth and store it all.  Integer sums:
+        // the order of the additions does not change the result.
+        // The receive slots lie in the staging area (early mode) or else in the operand
+        // ring, which is idle once this CTA's MMAs are done (acc_full): each CTA then
+        // tells the others so, and pushes once all of them have told it.
+        const int C = a.cluster;
         const uint32_t rank = cluster_ctarank();
         const int nch = (t.ncols + 15) / 16;
-        if (rank != 0) {
-          const bool go = a.cluster_early ||
-                          __all_sync(0xffffffffu, mbar_wait_cluster_bounded(
-                                                      done_bar, 0, abort_flag, a.status,
-                                                      kStatusClusterWait));
-          const uint32_t bar0 = map_to_rank(smem_u32(peer_bar), 0);
-          const uint32_t slot0 = map_to_rank(
-              smem_u32(ring + (static_cast<size_t>(rank) - 1) * TN * kXRows + row * TN), 0);
-          for (int c = 0; c < nch; ++c) {
-            uint32_t r[16];
-            tmem_acc16<TN>(t.taddr, c * 16, r);
-            if (go) {
-#pragma unroll
-              for (int v = 0; v < 4; ++v)
-                st_async_v4(slot0 + (c * 16 + 4 * v) * 4,
-                            make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]), bar0);
-            }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) release_acc(&acc_empty[acc]);
-        } else {
-          if (epi_tid == 0 && !a.cluster_early) {
-            mbar_arrive_expect_tx(peer_bar, static_cast<uint32_t>((a.cluster - 1) * nch * 16 * kXRows * 4));
-            for (int p = 1; p < a.cluster; ++p)
-              mbar_arrive_remote(map_to_rank(smem_u32(done_bar), static_cast<uint32_t>(p)));
-          }
-          const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(peer_bar, 0, abort_flag, a.status,
-                                                                      kStatusClusterWait));
-          for (int c0 = 0; c0 < t.ncols; c0 += 16) {
-            uint32_t r[16];
-            tmem_acc16<TN>(t.taddr, c0, r);
-            if (c0 + 16 >= t.ncols) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) release_acc(&acc_empty[acc]);
-            }
-            if (!got) continue;
-            for (int p = 1; p < a.cluster; ++p) {
-              const uint4 *src = reinterpret_cast<const uint4 *>(
-                  ring + (static_cast<size_t>(p) - 1) * TN * kXRows + row * TN + c0);
-#pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                const uint4 q = src[v];
-                r[4 * v] += q.x;
-                r[4 * v + 1] += q.y;
-                r[4 * v + 2] += q.z;
-                r[4 * v + 3] += q.w;
-              }
-            }
-            if (a.tma_out)
-              emit_swap16<TN>(a, &map_out, t, quarter, lane, c0, r, st);
-            else
-              epilogue_direct<TN>(a, t, row, c0, r);
-          }
+        const int owned_max = (TN / 16 + C - 1) / C;
+        const int sw = (row >> 1) & 3;  // 64-byte rows: 16-byte units swizzled over the banks
+        uint32_t *slots = reinterpret_cast<uint32_t *>(a.cluster_early ? staging : sx);
+        bool go = true;
+        if (!a.cluster_early) {
+          if (epi_tid == 0)
+            for (int p = 1; p < C; ++p)
+              mbar_arrive_remote(map_to_rank(smem_u32(done_bar), (rank + static_cast<uint32_t>(p)) % C));
+          go = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(done_bar, 0, abort_flag, a.status,
+                                                                 kStatusClusterWait));
         }
+        for (int c = 0; c < nch && go; ++c) {
+          const uint32_t owner = static_cast<uint32_t>(c % C);
+          if (owner == rank) continue;
+          uint32_t r[16];
+          tmem_acc16<TN>(t.taddr, c * 16, r);
+          const int sender = static_cast<int>(rank < owner ? rank : rank - 1);
+          const uint32_t bar = map_to_rank(smem_u32(peer_bar), owner);
+          const uint32_t dst = map_to_rank(
+              smem_u32(slots + ((static_cast<size_t>(sender) * owned_max + c / C) * kXRows + row) * 16), owner);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            st_async_v4(dst + ((v ^ sw) << 4), make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]),
+                        bar);
+        }
+        const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(peer_bar, 0, abort_flag, a.status,
+                                                                    kStatusClusterWait));
+        for (int c = static_cast<int>(rank); c < nch; c += C) {
+          uint32_t r[16];
+          tmem_acc16<TN>(t.taddr, c * 16, r);
+          if (!got) continue;
+          for (int p = 0; p < C - 1; ++p) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(
+                slots + ((static_cast<size_t>(p) * owned_max + c / C) * kXRows + row) * 16);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const uint4 q = src[v ^ sw];
+              r[4 * v] += q.x;
+              r[4 * v + 1] += q.y;
+              r[4 * v + 2] += q.z;
+              r[4 * v + 3] += q.w;
+            }
+          }
+          if (a.tma_out)
+            emit_swap16<TN>(a, &map_out, t, quarter, lane, c * 16, r, st);
+          else
+            epilogue_direct<TN>(a, t, row, c * 16, r);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release_acc(&acc_empty[acc]);
       } else if (whole) {
         if (!a.tma_out) {
           for (int c0 = 0; c0 < t.ncols; c0 += 16) {
@@ -1232,8 +1248,10 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
   tc_fence_before();
   __syncthreads();
   // A pair's CTAs leave together: neither exits while the other may still signal its
-  // barriers or the even CTA's MMAs may still read its shared memory.
-  if constexpr (kPair) cluster_sync();
+  // barriers or the even CTA's MMAs may still read its shared memory.  The CTAs of a
+  // split-K cluster likewise: none leaves while another may still push partial sums into
+  // its shared memory (a receiver whose wait gave up included).
+  if (kPair || a.cluster > 1) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     if constexpr (kPair)
@@ -1316,6 +1334,15 @@ static int max_stages_for(int y_rows, int smem_optin, int x_rows = kXRows) {
   const int stage = x_rows * kBK + y_rows * kBK;
   const int avail = smem_optin - static_cast<int>(smem_extra()) - 16;
   return std::max(1, std::min(16, avail / (stage + 16)));
+}
+
+// Bytes of partial sums one CTA of a split-K cluster of `c` receives: narrow tiles, the
+// leader gets (c-1) slots of M token rows x TN int32; swap_ab tiles, every CTA gets the
+// 16-column chunks it owns (one in c of TN/16) from each of the other (c-1), 128 rows x
+// 16 int32 per chunk.
+static long long cluster_recv_bytes(bool narrow, int M, int tn, int c) {
+  if (narrow) return static_cast<long long>(c - 1) * M * tn * 4;
+  return static_cast<long long>(c - 1) * ((tn / 16 + c - 1) / c) * 16 * kXRows * 4;
 }
 
 static bool valid_tok_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128 || t == 256; }
@@ -1468,12 +1495,11 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   if (split == 3) {
     if (!narrow && !t.swap_ab)
       return set_error(I8L_ENOTSUP, "cluster split-K takes swap_ab tiles or narrow 128 x 256 tiles");
-    // The leader's operand ring receives (cluster-1) partial-sum slots: TN x 128 int32
-    // (swap_ab tiles), or M token rows x TN int32 (narrow tiles).
+    // Narrow tiles: the leader's operand ring receives (cluster-1) slots of M token rows
+    // x TN int32.  swap_ab tiles: every CTA's ring receives, from each of the other
+    // (cluster-1), the 16-column chunks it owns (one in `cluster`, 128 rows x 16 int32).
     const long long ring = static_cast<long long>(t.stages) * (x_rows * kBK + p->tn * kBK);
-    const long long slot = narrow ? static_cast<long long>(M) * p->tn * 4
-                                  : static_cast<long long>(p->tn) * kXRows * 4;
-    auto fits = [&](int c) { return static_cast<long long>(c - 1) * slot <= ring; };
+    auto fits = [&](int c) { return cluster_recv_bytes(narrow, M, p->tn, c) <= ring; };
     int cs = t.cluster;
     if (cs <= 0) {
       cs = best_cluster(p->total_tiles, p->kblocks, ctas);
@@ -1717,13 +1743,10 @@ static int gemm_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, 
     a.act_src = aq->x;
     a.act_ld = aq->ldx;
   }
-  // Early cluster mode needs the (cluster-1) slots, each TN x 128 int32 apart, inside
-  // the leader's staging area, which plain stores leave unused.
-  if (p.cluster > 1 && !a.tma_out) {
-    const long long slot = p.narrow ? static_cast<long long>(M) * p.tn * 4
-                                    : static_cast<long long>(p.tn) * kXRows * 4;
-    a.cluster_early = static_cast<long long>(p.cluster - 1) * slot <= kStagingBytes ? 1 : 0;
-  }
+  // Early cluster mode needs every slot a CTA receives inside its staging area, which
+  // plain stores leave unused.
+  if (p.cluster > 1 && !a.tma_out)
+    a.cluster_early = cluster_recv_bytes(p.narrow, M, p.tn, p.cluster) <= kStagingBytes ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (p.tn) {
     case 16:

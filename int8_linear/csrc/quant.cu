@@ -26,6 +26,7 @@ namespace i8l {
 // Batches from which add_rmsnorm_quant runs two rows per CTA (measured on B200 at K=2048:
 // 11.0 -> 10.6 us at M=4096; at M=1024 the 512 CTAs were slower than 1024 one-row CTAs).
 constexpr int kNormTwoRowsMin = 2048;
+constexpr int kNormFourRowsMin = 4096;
 
 struct NormArgs {
   const void *x;
@@ -127,50 +128,60 @@ __global__ void __launch_bounds__(row_max_threads(NV, VW)) add_rmsnorm_quant_ker
   quantize_row<NV, VW>(x, a.K, a.q + row * a.ldq, a.scale + row, a.precise, red2);
 }
 
-// add_rmsnorm_quant_kernel for two rows per CTA (large batches, 16-byte vectors): every
-// thread owns the same columns in both rows as the one-row kernel gives it, and each
-// row's sums, maxima and roundings take exactly that kernel's steps, so the bits are
-// the same; the CTA count halves and each thread has twice the loads in flight.  The
-// last CTA of an odd batch has one row.
-template <int DT, int NV, int WDT>
-__global__ void __launch_bounds__(256) add_rmsnorm_quant_rows2_kernel(const NormArgs a, int M) {
+// add_rmsnorm_quant_kernel for R rows per CTA (large batches, 16-byte vectors): every
+// thread owns the same columns in each row as the one-row kernel gives it, and each
+// row's sums, maxima and roundings take exactly that kernel's steps, so the bits are the
+// same.  Every load (weights, then x and residual of every row) is issued before any
+// arithmetic or store, so all of them are in flight together (a residual store between
+// two rows' loads would hold the second row's loads back, as the compiler cannot tell
+// the store from the loads).  The last CTA may have fewer rows.
+template <int DT, int NV, int WDT, int R>
+__global__ void __launch_bounds__(256) add_rmsnorm_quant_rows_kernel(const NormArgs a, int M) {
   constexpr int VW = 8;
   pdl_launch_dependents();
   pdl_wait();
-  __shared__ float red[2][32], red2[2][32];
+  __shared__ float red[R][32], red2[R][32];
   using T = typename ActType<DT>::T;
-  const long long row0 = 2LL * blockIdx.x;
-  const int nrows = row0 + 1 < M ? 2 : 1;
-  float x[2][NV][VW], wv[NV][VW];
+  const long long row0 = static_cast<long long>(R) * blockIdx.x;
+  const int nrows = static_cast<int>(min(static_cast<long long>(R), M - row0));
+  float wv[NV][VW];
+  uint4 xr[R][NV], rr[R][NV];
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
     const int col = col_of<VW>(v);
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int i = 0; i < VW; ++i) x[r][v][i] = 0.f;
+    for (int r = 0; r < R; ++r) xr[r][v] = rr[r][v] = make_uint4(0u, 0u, 0u, 0u);
     if (col >= a.K) continue;
     load_weight_vec<VW>(a.w, WDT, col, a.w_vec != 0, wv[v]);
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
+    for (int r = 0; r < R; ++r) {
       if (r >= nrows) break;
       const long long row = row0 + r;
-      load_vec<DT, VW>(static_cast<const T *>(a.x) + row * a.ldx, col, x[r][v]);
-      if (a.res) {
+      xr[r][v] = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.x) + row * a.ldx + col);
+      if (a.res) rr[r][v] = *reinterpret_cast<const uint4 *>(static_cast<const T *>(a.res) + row * a.ldr + col);
+    }
+  }
+  float x[R][NV][VW];
+  float ss[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    ss[r] = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const T *h = reinterpret_cast<const T *>(&xr[r][v]);
+#pragma unroll
+      for (int i = 0; i < VW; ++i) x[r][v][i] = ActType<DT>::to_f32(h[i]);
+      const int col = col_of<VW>(v);
+      if (a.res && r < nrows && col < a.K) {
+        const T *g = reinterpret_cast<const T *>(&rr[r][v]);
         float rv[VW];
-        load_vec<DT, VW>(static_cast<const T *>(a.res) + row * a.ldr, col, rv);
+#pragma unroll
+        for (int i = 0; i < VW; ++i) rv[i] = ActType<DT>::to_f32(g[i]);
 #pragma unroll
         for (int i = 0; i < VW; i += 2)
           add2_rn(x[r][v][i], x[r][v][i + 1], x[r][v][i], x[r][v][i + 1], rv[i], rv[i + 1]);
-        store_vec<DT, VW>(static_cast<T *>(a.rout) + row * a.ldro, col, x[r][v]);
+        store_vec<DT, VW>(static_cast<T *>(a.rout) + (row0 + r) * a.ldro, col, x[r][v]);
       }
-    }
-  }
-  float ss[2] = {0.f, 0.f};
-#pragma unroll
-  for (int r = 0; r < 2; ++r)
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
       float sq[VW];
 #pragma unroll
       for (int i = 0; i < VW; i += 2)
@@ -178,10 +189,12 @@ __global__ void __launch_bounds__(256) add_rmsnorm_quant_rows2_kernel(const Norm
 #pragma unroll
       for (int i = 0; i < VW; ++i) ss[r] = __fadd_rn(ss[r], sq[i]);
     }
-  block_sum2(ss[0], ss[1], red);
-  float amax[2] = {0.f, 0.f};
+  }
+  block_reduce_n<R, false>(ss, red);
+  float amax[R];
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
+  for (int r = 0; r < R; ++r) {
+    amax[r] = 0.f;
     const float var = div_full(ss[r], static_cast<float>(a.K));
     const float rs = rsqrtf(__fadd_rn(var, a.eps));
 #pragma unroll
@@ -199,9 +212,9 @@ __global__ void __launch_bounds__(256) add_rmsnorm_quant_rows2_kernel(const Norm
       for (int i = 0; i < VW; ++i) amax[r] = fmaxf(amax[r], fabsf(x[r][v][i]));
     }
   }
-  block_max2(amax[0], amax[1], red2);
+  block_reduce_n<R, true>(amax, red2);
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
+  for (int r = 0; r < R; ++r) {
     if (r >= nrows) break;
     const long long row = row0 + r;
     if (threadIdx.x == 0)
@@ -458,15 +471,19 @@ extern "C" int i8l_add_rmsnorm_quant(const void *x, int64_t ldx, const void *res
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nv = rs.nv, th = rs.threads;
   cudaError_t err = cudaSuccess;
-  // Two rows per CTA for large batches of short rows (same bits, see the kernel).
+  // Several rows per CTA for large batches of short rows (same bits, see the kernel):
+  // 2 from kNormTwoRowsMin rows, 4 from kNormFourRowsMin when a row is one vector per thread.
   const bool two_rows = vec && nv <= 4 && th <= 256 && M >= kNormTwoRowsMin;
+  const bool four_rows = two_rows && nv == 1 && M >= kNormFourRowsMin;
 #define I8L_NORM_VEC(ADT, WDTV)                                                                     \
-  if (two_rows) {                                                                                   \
+  if (four_rows) {                                                                                  \
+    err = launch(add_rmsnorm_quant_rows_kernel<ADT, 1, WDTV, 4>, dim3((M + 3) / 4), dim3(th), 0, s, 1, a, M); \
+  } else if (two_rows) {                                                                            \
     switch (nv) {                                                                                   \
-      case 1: err = launch(add_rmsnorm_quant_rows2_kernel<ADT, 1, WDTV>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
-      case 2: err = launch(add_rmsnorm_quant_rows2_kernel<ADT, 2, WDTV>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
-      case 3: err = launch(add_rmsnorm_quant_rows2_kernel<ADT, 3, WDTV>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
-      default: err = launch(add_rmsnorm_quant_rows2_kernel<ADT, 4, WDTV>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
+      case 1: err = launch(add_rmsnorm_quant_rows_kernel<ADT, 1, WDTV, 2>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
+      case 2: err = launch(add_rmsnorm_quant_rows_kernel<ADT, 2, WDTV, 2>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
+      case 3: err = launch(add_rmsnorm_quant_rows_kernel<ADT, 3, WDTV, 2>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
+      default: err = launch(add_rmsnorm_quant_rows_kernel<ADT, 4, WDTV, 2>, dim3((M + 1) / 2), dim3(th), 0, s, 1, a, M); break; \
     }                                                                                               \
   } else {                                                                                          \
     I8L_DISPATCH_NV(nv, (err = launch(add_rmsnorm_quant_kernel<ADT, NV, 8, WDTV>, dim3(M), dim3(th), 0, s, 1, a))) \

@@ -82,6 +82,33 @@ __device__ __forceinline__ void block_max2(float &a, float &b, float (*red)[32])
   }
 }
 
+// block_sum / block_max of R rows at once (one barrier each), every row's value through
+// exactly the one-row reduction's steps.  `red` holds R x 32 floats, as `red` above.
+template <int R, bool kMax>
+__device__ __forceinline__ void block_reduce_n(float (&v)[R], float (*red)[32]) {
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, v[r], o);
+      v[r] = kMax ? fmaxf(v[r], t) : __fadd_rn(v[r], t);
+    }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (l == 0)
+#pragma unroll
+    for (int r = 0; r < R; ++r) red[r][w] = v[r];
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    v[r] = l < nw ? red[r][l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, v[r], o);
+      v[r] = kMax ? fmaxf(v[r], t) : __fadd_rn(v[r], t);
+    }
+  }
+}
+
 // Which row elements thread t owns: vector v (0..NV-1) covers columns
 // [(v*blockDim + t)*VW, +VW).  VW is 8 (16-byte vectors of 16-bit values) or 1.
 template <int VW>

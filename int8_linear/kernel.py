@@ -57,8 +57,8 @@ class Config:
             choice gives the same bits: 0 the library's choice, 1 whole tiles, 2
             stream-K over the SMs (reduced in a workspace), 3 cluster split-K (the CTAs
             of a thread-block cluster split a tile's K and reduce over distributed
-            shared memory; swap_ab tiles, as many CTAs as the leader's ring holds partial
-            sums for (up to 4 at 128 tokens, 2 at 256), or, without swap_ab, narrow
+            shared memory; swap_ab tiles, each CTA finishing one in `cluster` of the
+            tile's 16-column chunks from the others' partial sums, or, without swap_ab, narrow
             128 x 256 tiles for batches of <= 16 tokens: the weight on the MMA's N side,
             256 weight rows per MMA instruction), 4 CTA pairs (two SMs
             per 256 x 256 tile with 256-row tcgen05 MMAs; 128 x 256 tiles, no swap_ab),

@@ -84,7 +84,7 @@ def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
                 Config(mt, 0, split=5, stages=16)]
     if 64 < m <= 256:   # cluster split-K on the 128- and 256-token swap tiles
         tn = next(t for t in TOKEN_TILES if t >= m)
-        out += [Config(tn, 128, swap_ab=True, split=3, cluster=c) for c in (2, 3, 4)]
+        out += [Config(tn, 128, swap_ab=True, split=3, cluster=c) for c in (2, 3, 4, 6, 8)]
     if m >= 64:
         for bn in (128, 256):
             out += [Config(128, bn, split=1), Config(128, bn, split=2)]

@@ -201,9 +201,10 @@ def test_declines_narrow_tiles_for_large_batches():
 
 
 def test_declines_a_cluster_whose_partial_sums_do_not_fit():
-    a, w = ints((64, 2048), 1), ints((1024, 2048), 2)
+    # 16-token tiles: the one 16-column chunk goes to rank 0, 7 x 8 KB into a 2 x 18 KB ring
+    a, w = ints((16, 2048), 1), ints((1024, 2048), 2)
     with pytest.raises(NotSupported, match="ring"):
-        w8a8_mm(a, w.t(), one(), one(), config=Config(64, 128, split=3, cluster=8))
+        w8a8_mm(a, w.t(), one(), one(), config=Config(16, 128, split=3, cluster=8, stages=2))
 
 
 def test_declines_shapes_the_kernel_does_not_take():
@@ -424,22 +425,20 @@ def test_cuda_core_tiles_decline_larger_batches():
 
 @pytest.mark.parametrize("m", [65, 100, 128, 200, 256])
 @pytest.mark.parametrize("k,n", [(2048, 4096), (6144, 2048), (2048, 12288), (1040, 1000)])
-@pytest.mark.parametrize("cluster", [2, 3, 4])
-def test_cluster_split_wide_token_tiles(m, k, n, cluster):
-    """Cluster split-K on 128- and 256-token swap tiles: partial sums of 64 or 128 KB per
-    contributor into the leader's ring; declined when they do not fit."""
+@pytest.mark.parametrize("cluster", [2, 3, 4, 8])
+@pytest.mark.parametrize("store", [0, 1])
+def test_cluster_split_wide_token_tiles(m, k, n, cluster, store):
+    """Cluster split-K on 128- and 256-token swap tiles: each CTA finishes the 16-column
+    chunks c with c % cluster == its rank from the others' partial sums (ragged last
+    chunks when M is not a multiple of 16, ranks that own no live chunk)."""
     a, w = ints((m, k), 100 + m), ints((n, k), 101)
     g = torch.Generator().manual_seed(102)
     sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
     sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
-    cfg = Config(tok_tile(m), 128, swap_ab=True, split=3, cluster=cluster)
+    cfg = Config(tok_tile(m), 128, swap_ab=True, split=3, cluster=cluster, store=store)
     want = exact(a, w)
-    try:
-        got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
-    except NotSupported as e:
-        assert "cluster size" in str(e) and tok_tile(m) == 256, e
-        return
+    got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
     assert np.array_equal(np_(got), want)
     got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=cfg)
     assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), "bf16"))
