@@ -134,6 +134,18 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint4 v, uint
       : "memory");
 }
 
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this
+// CTA's shared memory into another CTA's of the cluster; its bytes complete the
+// transaction count of that CTA's mbarrier `cluster_bar`.  No multicast.
+__device__ __forceinline__ void bulk_copy_to_rank(uint32_t dst_cluster_addr, uint32_t src_smem, uint32_t bytes,
+                                                  uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster_addr),
+      "r"(src_smem), "r"(bytes), "r"(cluster_bar)
+      : "memory");
+}
+
 // Arrive on an mbarrier of another CTA of the cluster (release at cluster scope:
 // this thread's earlier shared-memory writes are visible to the waiter).
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {

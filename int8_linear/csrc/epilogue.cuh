@@ -28,6 +28,16 @@ __device__ __forceinline__ float dequant(int acc, float sa, float sb, float bias
   return v;
 }
 
+// Two 16-bit outputs (v0 in the low half), each rounded as out_bits16 rounds it.
+__device__ __forceinline__ uint32_t pack16x2(int dtype, float v0, float v1) {
+  uint32_t p;
+  if (dtype == I8L_BF16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v1), "f"(v0));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(v1), "f"(v0));
+  return p;
+}
+
 // Storage bits of one output value.
 __device__ __forceinline__ uint32_t out_bits16(int dtype, float v) {
   if (dtype == I8L_BF16) {

@@ -214,36 +214,108 @@ struct TileCtx {
   float s_row, b_row; // per TMEM lane: sa (normal) or sb, bias (swap)
 };
 
-// Plain stores of 16 accumulator values of TMEM lane `row`, accumulator columns
-// c0..c0+15 (output not TMA-addressable, or few output rows).  The scales and bias
-// come from the tile context, fetched before the accumulator was ready.
+// 16 consecutive per-column floats of the tile context (shared memory, 16-byte
+// aligned) into registers.  Loaded before any output is written: the compiler cannot
+// tell the output stores from these loads, so loads left between the stores would wait
+// for each one in turn (measured: ~1100 cycles per 16 values, against ~100).
+__device__ __forceinline__ void load16(const float *p, float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 f = reinterpret_cast<const float4 *>(p)[q];
+    v[4 * q] = f.x;
+    v[4 * q + 1] = f.y;
+    v[4 * q + 2] = f.z;
+    v[4 * q + 3] = f.w;
+  }
+}
+
+// Storage bits (16-bit outputs in the low half) of the 16 values of this thread's TMEM
+// lane, columns c0..c0+15 of a swap_ab tile: token scales per column, weight scale and
+// bias per lane.
+__device__ __forceinline__ void out_bits16x(const GemmArgs &a, const TileCtx &t, int c0, const uint32_t (&r)[16],
+                                            uint32_t (&bits)[16]) {
+  const bool has_bias = a.bias != nullptr;
+  float sa[16];
+  load16(t.s_col + c0, sa);
+  const bool wide = a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16;
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const int a0 = static_cast<int>(r[j]), a1 = static_cast<int>(r[j + 1]);
+    const float v0 = dequant(a0, sa[j], t.s_row, t.b_row, has_bias);
+    const float v1 = dequant(a1, sa[j + 1], t.s_row, t.b_row, has_bias);
+    if (wide) {
+      const uint32_t p = pack16x2(a.out_dtype, v0, v1);
+      bits[j] = p & 0xffffu;
+      bits[j + 1] = p >> 16;
+    } else {
+      bits[j] = out_bits32(a.out_dtype, a0, v0);
+      bits[j + 1] = out_bits32(a.out_dtype, a1, v1);
+    }
+  }
+}
+
+// Plain stores of the 16 values of this thread's TMEM lane, columns c0..c0+15 (output
+// not TMA-addressable, or few output rows).  The scales and bias come from the tile
+// context, fetched before the accumulator was ready; every value is computed before the
+// first store.
 template <int TN>
 __device__ __forceinline__ void epilogue_direct(const GemmArgs &a, const TileCtx &t, int row,
                                                 int c0, const uint32_t (&r)[16]) {
-  const bool raw = a.out_dtype == I8L_I32;
-  const bool has_bias = a.bias != nullptr;
+  uint32_t bits[16];
+  const bool wide = a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16;
   if (a.swap) {
     const int n = t.tx * kXRows + row;
     if (n >= a.N) return;
     const int m0 = t.ty * TN + c0;
+    out_bits16x(a, t, c0, r, bits);
+    const long long ldc = a.ldc;
+    const long long base = static_cast<long long>(m0) * ldc + n;
+    const int live = min(16, a.M - m0);
+    if (wide) {
+      uint16_t *o = static_cast<uint16_t *>(a.out) + base;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int m = m0 + j;
-      if (m < a.M) {
-        const int acc = static_cast<int>(r[j]);
-        const float v = raw ? 0.f : dequant(acc, t.s_col[c0 + j], t.s_row, t.b_row, has_bias);
-        store_elem(a.out, a.out_dtype, static_cast<long long>(m) * a.ldc + n, acc, v);
-      }
+      for (int j = 0; j < 16; ++j)
+        if (j < live) o[j * ldc] = static_cast<uint16_t>(bits[j]);
+    } else {
+      uint32_t *o = static_cast<uint32_t *>(a.out) + base;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < live) o[j * ldc] = bits[j];
     }
   } else {
     const int m = t.tx * kXRows + row;
     if (m >= a.M) return;
     const int n0 = t.ty * TN + c0;
+    const bool has_bias = a.bias != nullptr;
+    float sb[16], bias[16];
+    load16(t.s_col + c0, sb);
+    load16(t.b_col + c0, bias);
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const int a0 = static_cast<int>(r[j]), a1 = static_cast<int>(r[j + 1]);
+      const float v0 = dequant(a0, t.s_row, sb[j], bias[j], has_bias);
+      const float v1 = dequant(a1, t.s_row, sb[j + 1], bias[j + 1], has_bias);
+      if (wide) {
+        const uint32_t p = pack16x2(a.out_dtype, v0, v1);
+        bits[j] = p & 0xffffu;
+        bits[j + 1] = p >> 16;
+      } else {
+        bits[j] = out_bits32(a.out_dtype, a0, v0);
+        bits[j + 1] = out_bits32(a.out_dtype, a1, v1);
+      }
+    }
     const long long base = static_cast<long long>(m) * a.ldc + n0;
-    for (int j = 0; j < 16 && n0 + j < a.N; ++j) {
-      const int acc = static_cast<int>(r[j]);
-      const float v = raw ? 0.f : dequant(acc, t.s_row, t.s_col[c0 + j], t.b_col[c0 + j], has_bias);
-      store_elem(a.out, a.out_dtype, base + j, acc, v);
+    const int live = min(16, a.N - n0);
+    if (wide) {
+      uint16_t *o = static_cast<uint16_t *>(a.out) + base;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < live) o[j] = static_cast<uint16_t>(bits[j]);
+    } else {
+      uint32_t *o = static_cast<uint32_t *>(a.out) + base;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < live) o[j] = bits[j];
     }
   }
 }
@@ -394,24 +466,15 @@ template <int TN>
 __device__ __forceinline__ void emit_swap16(const GemmArgs &a, const CUtensorMap *map_out,
                                             const TileCtx &t, int quarter, int lane, int c0,
                                             const uint32_t (&r)[16], Staging &st) {
+  uint32_t bits[16];
+  out_bits16x(a, t, c0, r, bits);
   uint8_t *buf = st.acquire(lane);
-  const bool raw = a.out_dtype == I8L_I32;
-  const bool has_bias = a.bias != nullptr;
   if (a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16) {
-    uint16_t *b16 = reinterpret_cast<uint16_t *>(buf);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float v = dequant(static_cast<int>(r[j]), t.s_col[c0 + j], t.s_row, t.b_row, has_bias);
-      b16[j * 32 + lane] = static_cast<uint16_t>(out_bits16(a.out_dtype, v));
-    }
+    for (int j = 0; j < 16; ++j) reinterpret_cast<uint16_t *>(buf)[j * 32 + lane] = static_cast<uint16_t>(bits[j]);
   } else {
-    uint32_t *b32 = reinterpret_cast<uint32_t *>(buf);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int acc = static_cast<int>(r[j]);
-      const float v = raw ? 0.f : dequant(acc, t.s_col[c0 + j], t.s_row, t.b_row, has_bias);
-      b32[j * 32 + lane] = out_bits32(a.out_dtype, acc, v);
-    }
+    for (int j = 0; j < 16; ++j) reinterpret_cast<uint32_t *>(buf)[j * 32 + lane] = bits[j];
   }
   fence_proxy_async_smem();
   __syncwarp();
@@ -435,16 +498,20 @@ __device__ __forceinline__ void emit_normal(const GemmArgs &a, const CUtensorMap
   const bool has_bias = a.bias != nullptr;
   uint32_t p[16];
   if (a.out_dtype == I8L_BF16 || a.out_dtype == I8L_F16) {
+    // Column scales and bias by 16-byte loads; two outputs per conversion.
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int ca = c0 + 2 * j;
-      const float v0 = dequant(static_cast<int>(r0[2 * j]), t.s_row, t.s_col[ca], t.b_col[ca], has_bias);
-      const float v1 = dequant(static_cast<int>(r0[2 * j + 1]), t.s_row, t.s_col[ca + 1], t.b_col[ca + 1], has_bias);
-      p[j] = out_bits16(a.out_dtype, v0) | (out_bits16(a.out_dtype, v1) << 16);
-      const int cb = c0 + 16 + 2 * j;
-      const float w0 = dequant(static_cast<int>(r1[2 * j]), t.s_row, t.s_col[cb], t.b_col[cb], has_bias);
-      const float w1 = dequant(static_cast<int>(r1[2 * j + 1]), t.s_row, t.s_col[cb + 1], t.b_col[cb + 1], has_bias);
-      p[8 + j] = out_bits16(a.out_dtype, w0) | (out_bits16(a.out_dtype, w1) << 16);
+    for (int h = 0; h < 2; ++h) {
+      float sb[16], bias[16];
+      load16(t.s_col + c0 + 16 * h, sb);
+      if (has_bias) load16(t.b_col + c0 + 16 * h, bias);
+      const uint32_t (&r)[16] = h ? r1 : r0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v0 = dequant(static_cast<int>(r[2 * j]), t.s_row, sb[2 * j], has_bias ? bias[2 * j] : 0.f, has_bias);
+        const float v1 =
+            dequant(static_cast<int>(r[2 * j + 1]), t.s_row, sb[2 * j + 1], has_bias ? bias[2 * j + 1] : 0.f, has_bias);
+        p[8 * h + j] = pack16x2(a.out_dtype, v0, v1);
+      }
     }
   } else {
 #pragma unroll
@@ -1071,43 +1138,85 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
       } else if (a.cluster > 1) {
         // Cluster split-K, spread reduction.  Each CTA holds the partial sums of its k
         // range for the whole tile; 16-column chunk c is finished by CTA rank
-        // c % cluster.  Every CTA pushes the chunks it does not own into slot
-        // (sender) of the owner's receive area with st.async, which completes the
-        // owner's barrier by bytes, then adds the (cluster-1) received slots to its own
-        // chunks, dequantises and stores them.  Each SM thus takes in (cluster-1)/cluster
-        // of one tile's partial sums and stores 1/cluster of the tile, where a single
-        // leader would take in (cluster-1) tiles' worth and store it all.  Integer sums:
-        // the order of the additions does not change the result.
-        // The receive slots lie in the staging area (early mode) or else in the operand
-        // ring, which is idle once this CTA's MMAs are done (acc_full): each CTA then
-        // tells the others so, and pushes once all of them have told it.
+        // c % cluster.  Every CTA sends the chunks it does not own into slot (sender)
+        // of the owner's receive area, completing the owner's barrier by bytes, then
+        // adds the (cluster-1) received slots to its own chunks, dequantises and stores
+        // them.  Each SM thus takes in (cluster-1)/cluster of one tile's partial sums
+        // and stores 1/cluster of the tile, where a single leader would take in
+        // (cluster-1) tiles' worth and store it all.  Integer sums: the order of the
+        // additions does not change the result.  A chunk slot is 128 rows x 64 bytes,
+        // the four 16-byte units of a row XOR-swizzled by (row >> 1) & 3.
+        //   Early mode (the receive slots fit the staging area, free from the start
+        //   with plain stores): each thread pushes its rows with st.async.
+        //   Ring mode: the receive slots lie at the start of the operand ring, idle
+        //   once this CTA's MMAs are done (acc_full); each CTA tells the others so,
+        //   writes its outgoing chunks, grouped by owner, at the end of its own ring,
+        //   and one thread sends each owner's group with one bulk copy once every
+        //   other CTA has said its ring is free.
         const int C = a.cluster;
         const uint32_t rank = cluster_ctarank();
         const int nch = (t.ncols + 15) / 16;
-        const int owned_max = (TN / 16 + C - 1) / C;
         const int sw = (row >> 1) & 3;  // 64-byte rows: 16-byte units swizzled over the banks
+        constexpr int kChunkWords = kXRows * 16;  // one chunk slot: 8 KB
+        // Live chunks rank o owns; o's receive area holds slot (sender, j) at sender * that + j.
+        auto owned_by = [&](int o) { return nch > o ? (nch - o + C - 1) / C : 0; };
+        const int mine = owned_by(static_cast<int>(rank));
         uint32_t *slots = reinterpret_cast<uint32_t *>(a.cluster_early ? staging : sx);
-        bool go = true;
-        if (!a.cluster_early) {
+        if (a.cluster_early) {
+          for (int c = 0; c < nch; ++c) {
+            const uint32_t owner = static_cast<uint32_t>(c % C);
+            if (owner == rank) continue;
+            uint32_t r[16];
+            tmem_acc16<TN>(t.taddr, c * 16, r);
+            const int sender = static_cast<int>(rank < owner ? rank : rank - 1);
+            const uint32_t bar = map_to_rank(smem_u32(peer_bar), owner);
+            const uint32_t dst = map_to_rank(
+                smem_u32(slots + (static_cast<size_t>(sender) * owned_by(static_cast<int>(owner)) + c / C) *
+                                     kChunkWords + row * 16),
+                owner);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              st_async_v4(dst + ((v ^ sw) << 4),
+                          make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]), bar);
+          }
+        } else {
           if (epi_tid == 0)
             for (int p = 1; p < C; ++p)
               mbar_arrive_remote(map_to_rank(smem_u32(done_bar), (rank + static_cast<uint32_t>(p)) % C));
-          go = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(done_bar, 0, abort_flag, a.status,
-                                                                 kStatusClusterWait));
-        }
-        for (int c = 0; c < nch && go; ++c) {
-          const uint32_t owner = static_cast<uint32_t>(c % C);
-          if (owner == rank) continue;
-          uint32_t r[16];
-          tmem_acc16<TN>(t.taddr, c * 16, r);
-          const int sender = static_cast<int>(rank < owner ? rank : rank - 1);
-          const uint32_t bar = map_to_rank(smem_u32(peer_bar), owner);
-          const uint32_t dst = map_to_rank(
-              smem_u32(slots + ((static_cast<size_t>(sender) * owned_max + c / C) * kXRows + row) * 16), owner);
+          const int out_chunks = nch - mine;
+          uint32_t *out = reinterpret_cast<uint32_t *>(staging) - static_cast<size_t>(out_chunks) * kChunkWords;
+          int group = 0;  // first outgoing slot of the current owner's group
+          for (int o = 0; o < C; ++o) {
+            if (o == static_cast<int>(rank)) continue;
+            for (int j = 0, c = o; c < nch; ++j, c += C) {
+              uint32_t r[16];
+              tmem_acc16<TN>(t.taddr, c * 16, r);
+              uint4 *dst = reinterpret_cast<uint4 *>(out + static_cast<size_t>(group + j) * kChunkWords + row * 16);
 #pragma unroll
-          for (int v = 0; v < 4; ++v)
-            st_async_v4(dst + ((v ^ sw) << 4), make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]),
-                        bar);
+              for (int v = 0; v < 4; ++v)
+                dst[v ^ sw] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+            }
+            group += owned_by(o);
+          }
+          fence_proxy_async_smem();  // generic-proxy stores -> source of the bulk copies
+          named_bar_sync(1, kEpiWarps * 32);
+          if (epi_tid == 0 && mbar_wait_cluster_bounded(done_bar, 0, abort_flag, a.status, kStatusClusterWait)) {
+            group = 0;
+            for (int o = 0; o < C; ++o) {
+              if (o == static_cast<int>(rank)) continue;
+              const int n_o = owned_by(o);
+              if (n_o > 0) {
+                const int sender = static_cast<int>(rank) < o ? static_cast<int>(rank) : static_cast<int>(rank) - 1;
+                bulk_copy_to_rank(
+                    map_to_rank(smem_u32(slots + static_cast<size_t>(sender) * n_o * kChunkWords),
+                                static_cast<uint32_t>(o)),
+                    smem_u32(out + static_cast<size_t>(group) * kChunkWords),
+                    static_cast<uint32_t>(n_o) * kChunkWords * 4,
+                    map_to_rank(smem_u32(peer_bar), static_cast<uint32_t>(o)));
+              }
+              group += n_o;
+            }
+          }
         }
         const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(peer_bar, 0, abort_flag, a.status,
                                                                     kStatusClusterWait));
@@ -1117,7 +1226,7 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
           if (!got) continue;
           for (int p = 0; p < C - 1; ++p) {
             const uint4 *src = reinterpret_cast<const uint4 *>(
-                slots + ((static_cast<size_t>(p) * owned_max + c / C) * kXRows + row) * 16);
+                slots + (static_cast<size_t>(p) * mine + c / C) * kChunkWords + row * 16);
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const uint4 q = src[v ^ sw];
@@ -1213,20 +1322,17 @@ __global__ void __launch_bounds__(kThreads, (TN <= 64 || kVar == kVarNarrow) ? 2
           const int step = (!a.swap && wide && a.tma_out) ? 32 : 16;
           for (int c0 = 0; c0 < t.ncols; c0 += step) {
             uint32_t r0[16], r1[16];
+            // All loads first, then the zeroing stores: the accesses are ordered as
+            // written, so interleaving them would serialise 16-32 L2 round trips.
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              int *p = ws + (c0 + j) * kXRows + row;
-              r0[j] = static_cast<uint32_t>(ld_cg_s32(p));
-              st_cg_s32(p, 0);
-            }
+            for (int j = 0; j < 16; ++j) r0[j] = static_cast<uint32_t>(ld_cg_s32(ws + (c0 + j) * kXRows + row));
             if (step == 32) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                int *p = ws + (c0 + 16 + j) * kXRows + row;
-                r1[j] = static_cast<uint32_t>(ld_cg_s32(p));
-                st_cg_s32(p, 0);
-              }
+              for (int j = 0; j < 16; ++j)
+                r1[j] = static_cast<uint32_t>(ld_cg_s32(ws + (c0 + 16 + j) * kXRows + row));
             }
+#pragma unroll
+            for (int j = 0; j < step; ++j) st_cg_s32(ws + (c0 + j) * kXRows + row, 0);
             if (!a.tma_out)
               epilogue_direct<TN>(a, t, row, c0, r0);
             else if (a.swap)
@@ -1336,13 +1442,26 @@ static int max_stages_for(int y_rows, int smem_optin, int x_rows = kXRows) {
   return std::max(1, std::min(16, avail / (stage + 16)));
 }
 
-// Bytes of partial sums one CTA of a split-K cluster of `c` receives: narrow tiles, the
-// leader gets (c-1) slots of M token rows x TN int32; swap_ab tiles, every CTA gets the
-// 16-column chunks it owns (one in c of TN/16) from each of the other (c-1), 128 rows x
-// 16 int32 per chunk.
+// Most bytes of partial sums one CTA of a split-K cluster of `c` receives: narrow tiles,
+// the leader gets (c-1) slots of M token rows x TN int32; swap_ab tiles, every CTA gets
+// the 16-column chunks it owns (one in c of TN/16, rank 0 the most) from each of the
+// other (c-1), 128 rows x 16 int32 per chunk.
 static long long cluster_recv_bytes(bool narrow, int M, int tn, int c) {
   if (narrow) return static_cast<long long>(c - 1) * M * tn * 4;
   return static_cast<long long>(c - 1) * ((tn / 16 + c - 1) / c) * 16 * kXRows * 4;
+}
+
+// Ring bytes a CTA of a split-K cluster of `c` swap_ab tiles needs in ring mode: its
+// incoming slots ((c-1) senders x the chunks it owns) at the start and its outgoing
+// chunks (those it does not own) at the end; the most over the ranks.
+static long long cluster_ring_bytes(int tn, int c) {
+  const int nch = tn / 16;
+  long long worst = 0;
+  for (int r = 0; r < c; ++r) {
+    const int own = nch > r ? (nch - r + c - 1) / c : 0;
+    worst = std::max(worst, static_cast<long long>((c - 1) * own + (nch - own)) * 16 * kXRows * 4);
+  }
+  return worst;
 }
 
 static bool valid_tok_tile(int t) { return t == 16 || t == 32 || t == 64 || t == 128 || t == 256; }
@@ -1499,7 +1618,9 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
     // x TN int32.  swap_ab tiles: every CTA's ring receives, from each of the other
     // (cluster-1), the 16-column chunks it owns (one in `cluster`, 128 rows x 16 int32).
     const long long ring = static_cast<long long>(t.stages) * (x_rows * kBK + p->tn * kBK);
-    auto fits = [&](int c) { return cluster_recv_bytes(narrow, M, p->tn, c) <= ring; };
+    auto fits = [&](int c) {
+      return (narrow ? cluster_recv_bytes(true, M, p->tn, c) : cluster_ring_bytes(p->tn, c)) <= ring;
+    };
     int cs = t.cluster;
     if (cs <= 0) {
       cs = best_cluster(p->total_tiles, p->kblocks, ctas);

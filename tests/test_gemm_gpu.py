@@ -438,6 +438,10 @@ def test_cluster_split_wide_token_tiles(m, k, n, cluster, store):
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
     cfg = Config(tok_tile(m), 128, swap_ab=True, split=3, cluster=cluster, store=store)
     want = exact(a, w)
+    if tok_tile(m) == 256 and cluster == 8:   # 7 x 2 chunks in + 14 out: 224 KB > the 192 KB ring
+        with pytest.raises(NotSupported, match="ring"):
+            w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
+        return
     got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
     assert np.array_equal(np_(got), want)
     got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=cfg)
