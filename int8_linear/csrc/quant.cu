@@ -23,9 +23,11 @@
 
 namespace i8l {
 
-// Batches from which add_rmsnorm_quant runs two rows per CTA (measured on B200 at K=2048:
-// 11.0 -> 10.6 us at M=4096; at M=1024 the 512 CTAs were slower than 1024 one-row CTAs).
-constexpr int kNormTwoRowsMin = 2048;
+// Batches from which add_rmsnorm_quant runs several rows per CTA (measured on B200 at
+// K=2048, µs per call: M=2048 6.47 with one row per CTA against 6.88 with two; M=4096
+// 11.4-11.7 with two or four rows against 11.6-12.1 with one; eight rows per CTA took
+// twice as long).
+constexpr int kNormTwoRowsMin = 4096;
 constexpr int kNormFourRowsMin = 4096;
 
 struct NormArgs {
