@@ -545,7 +545,7 @@ def run_ours(args, world, rank, dev):
 
     from int8_linear import w8a8_mm
 
-    peak = int8_peak_probe(dev) if world == 1 else None
+    peak = int8_peak_probe(dev)  # every rank on its own GPU; the line reports rank 0's
     pk = peaks(peak["peak"] if peak else None)
     layers, acts = build_operands(args.model, world, rank, dev)
     cases = sweep_cases(layers)
