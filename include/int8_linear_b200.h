@@ -340,6 +340,12 @@ typedef struct i8l_peer_comm {
   int64_t slot_bytes;         /* bytes per (parity, source) inbox slot, multiple of 16 */
   int32_t max_rows;           /* rows per call (and epoch counters)                  */
   uint64_t timeout_ns;        /* bound on each wait for a peer (0 = 2 s)             */
+  /* Rows per call from which the row-parallel exchanges (i8l_tp_allreduce_*) run two-shot:
+   * each GPU sums its 1/world of the columns from every GPU's partials (reduce-scatter)
+   * and sends the sums to the others (all-gather), (world-1)/world x 16 bytes per column
+   * sent instead of (world-1) x 8.  0 = the library's choice (64 rows with 4 or more
+   * GPUs, else one-shot), < 0 = always one-shot.  Needs N % (4 x world) == 0. */
+  int32_t two_shot_rows;
 } i8l_peer_comm;
 
 /* Bytes of one exchange buffer: 2 parities x world source slots (0 for a slot that is

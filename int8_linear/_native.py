@@ -39,7 +39,8 @@ class I8LPeerComm(ctypes.Structure):
 
     _fields_ = [("bases", ctypes.c_void_p * MAX_RANKS), ("epochs", ctypes.c_void_p),
                 ("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("slot_bytes", ctypes.c_int64),
-                ("max_rows", ctypes.c_int32), ("timeout_ns", ctypes.c_uint64)]
+                ("max_rows", ctypes.c_int32), ("timeout_ns", ctypes.c_uint64),
+                ("two_shot_rows", ctypes.c_int32)]
 
 
 _lib = None

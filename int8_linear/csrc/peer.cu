@@ -50,6 +50,7 @@ struct PeerArgs {
   long long slot_bytes;      // bytes of one (parity, source) inbox slot
   int max_rows;
   unsigned long long timeout_ns;
+  int two_shot;              // row-parallel sums: reduce-scatter + all-gather (see exchange_groups)
 };
 
 // inbox[parity][src] of GPU `dst`.
@@ -141,6 +142,61 @@ __device__ __forceinline__ void receive_group(const PeerArgs &p, size_t off, int
   }
 }
 
+// Sums G 4-column groups of one row over the GPUs: group g (columns cols[g]..+3, skipped
+// when cols[g] >= N) of this GPU's partials is v[g] on entry and the sum on return.
+// One-shot: every GPU sends its groups to every other GPU and adds what arrives.
+// Two-shot: the row's columns are split into `world` equal slices; the GPU that owns a
+// group's slice receives that group from every other GPU and adds it (reduce-scatter),
+// then sends the sum to every other GPU, which takes it as is (all-gather).  A group
+// travels into inbox[parity][src] at its column offset in both phases: in the first
+// only into the owner's slice columns, in the second only from the owner into its own
+// slice columns, so the two never write the same words of a call.
+template <int G>
+__device__ __forceinline__ void exchange_groups(const PeerArgs &p, size_t row_off, const int (&cols)[G],
+                                                int4 (&v)[G], int N, unsigned e, bool &ok) {
+  if (!p.two_shot) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      if (cols[g] < N) send_group(p, row_off + static_cast<size_t>(cols[g]) * 8, v[g], e);
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      if (cols[g] < N) receive_group(p, row_off + static_cast<size_t>(cols[g]) * 8, v[g], e, ok);
+    return;
+  }
+  const unsigned par = e & 1u;
+  const int slice = N / p.world;
+  // phase 1: each group not in this GPU's slice to its owner
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (cols[g] >= N) continue;
+    const int o = cols[g] / slice;
+    if (o == p.rank) continue;
+    uint8_t *dst = inbox(p, o, par, p.rank) + row_off + static_cast<size_t>(cols[g]) * 8;
+    st_ll(dst, static_cast<unsigned>(v[g].x), static_cast<unsigned>(v[g].y), e);
+    st_ll(dst + 16, static_cast<unsigned>(v[g].z), static_cast<unsigned>(v[g].w), e);
+  }
+  // this GPU's slice: add every other GPU's group, then send the sum to each of them
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (cols[g] >= N || cols[g] / slice != p.rank) continue;
+    const size_t off = row_off + static_cast<size_t>(cols[g]) * 8;
+    receive_group(p, off, v[g], e, ok);
+    send_group(p, off, v[g], e);
+  }
+  // phase 2: the other slices' sums from their owners
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (cols[g] >= N) continue;
+    const int o = cols[g] / slice;
+    if (o == p.rank) continue;
+    const uint8_t *src = inbox(p, p.rank, par, o) + row_off + static_cast<size_t>(cols[g]) * 8;
+    const uint2 lo = wait_ll(p, src, e, ok);
+    const uint2 hi = wait_ll(p, src + 16, e, ok);
+    v[g] = make_int4(static_cast<int>(lo.x), static_cast<int>(lo.y), static_cast<int>(hi.x),
+                     static_cast<int>(hi.y));
+  }
+}
+
 // ------------------------------------------------------------------ all-reduce + dequant
 
 struct ReduceArgs {
@@ -186,16 +242,10 @@ __device__ __forceinline__ void reduce_row(const ReduceArgs &a, int row, unsigne
     acc[v] = make_int4(0, 0, 0, 0);
     if (c < a.N) acc[v] = ld_cg_i4(a.partial + static_cast<long long>(row) * a.ldp + c);
   }
+  int cols[NV];
 #pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int c = (v * blockDim.x + threadIdx.x) * 4;
-    if (c < a.N) send_group(a.p, off + static_cast<size_t>(c) * 8, acc[v], e);
-  }
-#pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int c = (v * blockDim.x + threadIdx.x) * 4;
-    if (c < a.N) receive_group(a.p, off + static_cast<size_t>(c) * 8, acc[v], e, ok);
-  }
+  for (int v = 0; v < NV; ++v) cols[v] = (v * blockDim.x + threadIdx.x) * 4;
+  exchange_groups<NV>(a.p, off, cols, acc, a.N, e, ok);
 }
 
 template <int NV>
@@ -280,20 +330,22 @@ __global__ void __launch_bounds__(row_max_threads(NV, 8)) tp_allreduce_norm_kern
         acc[v][1] = ld_cg_i4(src + 4);
       }
     }
+    {
+      int cols[2 * NV];
+      int4 grp[2 * NV];
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const int c = col_of<8>(v);
-      if (c < N) {
-        send_group(p, off + static_cast<size_t>(c) * 8, acc[v][0], e);
-        send_group(p, off + static_cast<size_t>(c + 4) * 8, acc[v][1], e);
+      for (int v = 0; v < NV; ++v) {
+        const int c = col_of<8>(v);
+        cols[2 * v] = c < N ? c : N;
+        cols[2 * v + 1] = c < N ? c + 4 : N;
+        grp[2 * v] = acc[v][0];
+        grp[2 * v + 1] = acc[v][1];
       }
-    }
+      exchange_groups<2 * NV>(p, off, cols, grp, N, e, ok);
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const int c = col_of<8>(v);
-      if (c < N) {
-        receive_group(p, off + static_cast<size_t>(c) * 8, acc[v][0], e, ok);
-        receive_group(p, off + static_cast<size_t>(c + 4) * 8, acc[v][1], e, ok);
+      for (int v = 0; v < NV; ++v) {
+        acc[v][0] = grp[2 * v];
+        acc[v][1] = grp[2 * v + 1];
       }
     }
     // 2. dequant to the activation dtype (the layer output h), + residual, RMSNorm
@@ -465,6 +517,13 @@ static int peer_args(const i8l_peer_comm *c, PeerArgs *p, int rows, long long ro
   return I8L_OK;
 }
 
+// Whether a row-parallel exchange of M rows of N int32 runs two-shot (the comm's
+// two_shot_rows; 0 = from 64 rows with 4 or more GPUs).
+static void set_two_shot(const i8l_peer_comm *c, PeerArgs *p, int M, int N) {
+  const int rows = c->two_shot_rows == 0 ? (c->world >= 4 ? 64 : -1) : c->two_shot_rows;
+  p->two_shot = (rows > 0 && M >= rows && c->world > 1 && N % (4 * c->world) == 0) ? 1 : 0;
+}
+
 // CTAs: one per row up to the SM count (all resident at once; see the file comment),
 // and never more than the epoch counters the communicator holds.
 static int peer_grid(const i8l_peer_comm *c, int M) {
@@ -548,6 +607,7 @@ extern "C" int i8l_tp_allreduce_dequant(const i8l_peer_comm *comm, const int32_t
   ReduceArgs a{};
   int e = peer_args(comm, &a.p, M, static_cast<long long>(N) * 8);
   if (e) return e;
+  set_two_shot(comm, &a.p, M, N);
   a.partial = partial;
   a.ldp = ldp;
   a.sa = sa;
@@ -609,6 +669,7 @@ extern "C" int i8l_tp_allreduce_add_rmsnorm_quant(
   ReduceNormArgs a{};
   int e = peer_args(comm, &a.r.p, M, static_cast<long long>(N) * 8);
   if (e) return e;
+  set_two_shot(comm, &a.r.p, M, N);
   a.r.partial = partial;
   a.r.ldp = ldp;
   a.r.sa = sa;

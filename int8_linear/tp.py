@@ -77,10 +77,12 @@ class PeerComm:
     sends per call (8 bytes per int32 value of a row-parallel all-reduce, as each travels
     with the call's epoch; 16 bytes per row for an absmax), `max_rows` the rows
     per call.  Calls that exceed them raise NotSupported (the callers fall back to NCCL).
-    Every GPU of the group must make the same calls in the same order."""
+    `two_shot_rows`: batches from which the row-parallel sums run as reduce-scatter +
+    all-gather instead of one all-to-all (0: the library's choice, 64 rows from 4 GPUs;
+    negative: never).  Every GPU of the group must make the same calls in the same order."""
 
     def __init__(self, group=None, slot_bytes: int = 8 << 20, max_rows: int = 4096,
-                 timeout_ns: int = 0, device: torch.device | None = None):
+                 timeout_ns: int = 0, device: torch.device | None = None, two_shot_rows: int = 0):
         lib = _native.load()
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
@@ -115,6 +117,7 @@ class PeerComm:
         self.desc.rank, self.desc.world = self.rank, self.world
         self.desc.slot_bytes, self.desc.max_rows = slot_bytes, max_rows
         self.desc.timeout_ns = timeout_ns
+        self.desc.two_shot_rows = two_shot_rows
         self.slot_bytes, self.max_rows = slot_bytes, max_rows
         dist.barrier(group=group)   # every buffer is mapped before any GPU signals into it
 

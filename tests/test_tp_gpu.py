@@ -45,7 +45,8 @@ def _worker(rank, path, m, mode, q):
     comm = None
     try:
         set_pdl(True)
-        comm = PeerComm(device=dev) if mode == "peer" else None
+        comm = (PeerComm(device=dev, two_shot_rows=1 if mode == "peer2" else 0)
+                if mode.startswith("peer") else None)
         tpd = TPStandinDecoder(m, rank, WORLD, layers=3, device=dev, comm=comm)
         eager = tpd.step()
         g = tpd.capture()
@@ -81,15 +82,16 @@ def _run(target, *args):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason=f"needs {WORLD} GPUs")
-@pytest.mark.parametrize("mode", ["nccl", "peer"])
+@pytest.mark.parametrize("mode", ["nccl", "peer", "peer2"])
 @pytest.mark.parametrize("m", [1, 16])
 def test_tp_standin_equals_one_gpu(m, mode):
+    """peer2: the NVLink exchange kernels with the row-parallel sums forced two-shot."""
     for rank, ok, same in _run(_worker, m, mode):
         assert ok, f"rank {rank}: graph replay differs from eager"
         assert same, f"rank {rank}: TP output differs from the one-GPU stand-in"
 
 
-def _ops_worker(rank, path, q):
+def _ops_worker(rank, path, two_shot, q):
     import torch.distributed as dist
 
     from int8_linear import fused_quant as fq
@@ -100,7 +102,7 @@ def _ops_worker(rank, path, q):
     comm = None
     fails = []
     try:
-        comm = tp.PeerComm(device=dev)
+        comm = tp.PeerComm(device=dev, two_shot_rows=1 if two_shot else -1)
         one = torch.ones(1, device=dev)
         for m, k, n in [(1, 2048, 2048), (5, 1024, 4096), (64, 6144, 2048), (200, 512, 1024)]:
             g = torch.Generator(device=dev).manual_seed(m * 7 + n)
@@ -150,8 +152,10 @@ def _ops_worker(rank, path, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason=f"needs {WORLD} GPUs")
-def test_peer_exchange_ops_equal_one_gpu():
-    """Every exchange kernel on two GPUs gives what one GPU gives on the whole row."""
-    for rank, fails, status in _run(_ops_worker):
+@pytest.mark.parametrize("two_shot", [False, True])
+def test_peer_exchange_ops_equal_one_gpu(two_shot):
+    """Every exchange kernel on two GPUs gives what one GPU gives on the whole row, with
+    the row-parallel sums one-shot and two-shot (reduce-scatter + all-gather)."""
+    for rank, fails, status in _run(_ops_worker, two_shot):
         assert status == 0, f"rank {rank}: status word {status}"
         assert not fails, f"rank {rank}: {fails}"
