@@ -343,7 +343,7 @@ typedef struct i8l_peer_comm {
   /* Rows per call from which the row-parallel exchanges (i8l_tp_allreduce_*) run two-shot:
    * each GPU sums its 1/world of the columns from every GPU's partials (reduce-scatter)
    * and sends the sums to the others (all-gather), (world-1)/world x 16 bytes per column
-   * sent instead of (world-1) x 8.  0 = the library's choice (64 rows with 4 or more
+   * sent instead of (world-1) x 8.  0 = the library's choice (16 rows with 4 or more
    * GPUs, else one-shot), < 0 = always one-shot.  Needs N % (4 x world) == 0. */
   int32_t two_shot_rows;
 } i8l_peer_comm;

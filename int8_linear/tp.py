@@ -78,7 +78,7 @@ class PeerComm:
     with the call's epoch; 16 bytes per row for an absmax), `max_rows` the rows
     per call.  Calls that exceed them raise NotSupported (the callers fall back to NCCL).
     `two_shot_rows`: batches from which the row-parallel sums run as reduce-scatter +
-    all-gather instead of one all-to-all (0: the library's choice, 64 rows from 4 GPUs;
+    all-gather instead of one all-to-all (0: the library's choice, 16 rows from 4 GPUs;
     negative: never).  Every GPU of the group must make the same calls in the same order."""
 
     def __init__(self, group=None, slot_bytes: int = 8 << 20, max_rows: int = 4096,
