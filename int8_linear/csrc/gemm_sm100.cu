@@ -1593,10 +1593,7 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   p->cluster = 1;
   if (split == 0) {
     // Decode tiles with fewer tiles than SMs: split K inside thread-block clusters
-    // when that keeps most SMs streaming; many tiles: whole tiles unless the last
-    // wave would leave many SMs idle, then stream-K.
-    const int waves = (p->total_tiles + ctas - 1) / ctas;
-    const double wave_eff = static_cast<double>(p->total_tiles) / (static_cast<double>(waves) * ctas);
+    // when that keeps most SMs streaming; otherwise whole tiles.
     if (t.swap_ab && p->tn <= 64 && p->total_tiles < ctas) {
       // Cluster split-K when it fills clearly more SMs than whole tiles, else whole tiles.
       const int cs = best_cluster(p->total_tiles, p->kblocks, ctas);
@@ -1605,10 +1602,20 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
       // Decode tiles fit two per SM: one CTA per tile, all resident at once.
       split = 1;
       ctas = p->total_tiles;
-    } else if (wave_eff >= 0.6 || p->total_tiles >= 4 * ctas) {
-      split = 1;  // the stream-K fix-up costs more than the idle share of the last wave
+    } else if (t.swap_ab && p->total_tiles < ctas && t.cluster <= 0) {
+      // 128- and 256-token tiles on fewer tiles than SMs: cluster split-K while each CTA
+      // keeps at least 8 k-blocks (measured on B200 at 128 tokens: down, 48 k-blocks,
+      // cluster 4 12.2 against 19.2 µs whole; qkv, 16 k-blocks, cluster 2 within 6% of
+      // whole tiles, cluster 4 50% slower).
+      int cs = best_cluster(p->total_tiles, p->kblocks, ctas);
+      while (cs > 1 && p->kblocks / cs < 8) --cs;
+      split = cs > 1 ? 3 : 1;
+      t.cluster = cs;
     } else {
-      split = 2;
+      // Whole tiles.  Stream-K (split 2, on request) measured slower on every shape
+      // tried on B200: 53.7 against 29.9 µs at 4096 x 4096 x 2048, 22.5 against 9.4 µs
+      // at 128 x 4096 x 2048.
+      split = 1;
     }
   }
   if (split == 3) {

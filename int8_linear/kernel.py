@@ -148,9 +148,10 @@ def default_config(m: int, n: int, k: int) -> Config:
     16 MB, take the CUDA-core tiles (split 5; measured faster than every tensor-core tiling
     there on B200).  Other decode batches (M <= 256) put the weight on the 128-row
     MMA side and the tokens on the narrow side, the smallest token tile that holds
-    M; larger batches use 128 x 256 tiles.  The library then splits K when whole
-    tiles would leave SMs idle: inside thread-block clusters for decode tiles, by
-    stream-K otherwise.  Prefill with K >= 4096 uses CTA pairs (split 4).  Batches of
+    M; larger batches use 128 x 256 tiles.  The library then splits K inside
+    thread-block clusters when decode tiles would leave SMs idle (never by stream-K,
+    which measured slower on every shape tried).  Prefill with K >= 4096 uses CTA pairs
+    (split 4).  Batches of
     one or two tokens on moderate weights (K 1024..6144, N <= 8192) take narrow tiles
     instead: 256 weight rows per MMA, K split over a cluster of up to 8 CTAs with at
     least two 128-wide k-blocks each (measured faster there on B200; larger weights
