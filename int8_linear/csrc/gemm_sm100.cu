@@ -1590,6 +1590,7 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   const long long total_iters = static_cast<long long>(p->total_tiles) * p->kblocks;
   int ctas = t.ctas > 0 ? t.ctas : di.sms;
   int split = t.split;
+  bool auto_cluster = t.cluster <= 0;  // cluster size left to the library (shrunk to fit below)
   p->cluster = 1;
   if (split == 0) {
     // Decode tiles with fewer tiles than SMs: split K inside thread-block clusters
@@ -1629,10 +1630,9 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
       return (narrow ? cluster_recv_bytes(true, M, p->tn, c) : cluster_ring_bytes(p->tn, c)) <= ring;
     };
     int cs = t.cluster;
-    if (cs <= 0) {
-      cs = best_cluster(p->total_tiles, p->kblocks, ctas);
+    if (cs <= 0) cs = best_cluster(p->total_tiles, p->kblocks, ctas);
+    if (auto_cluster)
       while (cs > 1 && !fits(cs)) --cs;
-    }
     if (cs < 1 || cs > 8 || cs > p->kblocks || !fits(cs))
       return set_error(I8L_ENOTSUP,
                        "cluster size %d outside [1, min(8, k-blocks=%d)] or its partial sums "

@@ -446,3 +446,14 @@ def test_cluster_split_wide_token_tiles(m, k, n, cluster, store):
     assert np.array_equal(np_(got), want)
     got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=cfg)
     assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), "bf16"))
+
+
+@pytest.mark.parametrize("m", [65, 128, 200, 256])
+@pytest.mark.parametrize("k,n", [(6144, 256), (2048, 512), (14336, 512), (4096, 768), (6144, 1536), (2048, 256)])
+def test_default_tiles_of_untuned_shapes(m, k, n):
+    """Tensor-parallel shards and other shapes outside the tile table take the library's
+    own choice (cluster split-K sized to fit the ring for 128/256-token tiles on few
+    tiles): it must run and be exact."""
+    a, w = ints((m, k), 300 + m), ints((n, k), 301)
+    assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True)), exact(a, w))
+
