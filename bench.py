@@ -18,9 +18,9 @@ L2-cold.  `value` is microseconds per sweep (one GEMM of each case), device time
 `e2e` is the same sweep through the public API w8a8_mm, eagerly, with each step's int8
 activations and scales copied in from pinned host memory and every output copied back.
 
-The final line keeps to a few KB (the driver reads the tail of stdout); the per-shape
-table, the L2-warm timings and the full quantiser table go to --detail (default
-gpurun_out/bench_detail_n<N>.json).
+The final line keeps to a few KB (only the tail of stdout is read); the per-shape
+table, the L2-warm timings and the full quantiser table go to the --detail file
+(default: bench_detail_n<N>.json in the run's output folder, see detail_path).
 
 Under torchrun (N > 1) each rank runs its column shard (N/g output columns) of every
 layer, independently; the NCCL all-gather of the shards is timed separately and
