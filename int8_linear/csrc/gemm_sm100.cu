@@ -20,9 +20,12 @@
 // tokens); for prefill shapes the activation is X.
 //
 // Work split: the (tile, k-block) iteration space is divided among the CTAs.
-// Whole tiles go round-robin first; the tail (the last partial wave plus one
-// full wave) is divided into equal contiguous k-block ranges (stream-K), so
-// some tiles are computed in pieces by several CTAs.  Each piece adds its int32
+// Whole tiles go round-robin (the library's choice for prefill and for decode tiles
+// that fill the SMs); cluster split-K shares one tile's k-blocks among the CTAs of a
+// thread-block cluster (decode tiles on few tiles, reduced over distributed shared
+// memory, see the epilogue).  On request (split 2, stream-K) the tail (the last
+// partial wave plus one full wave) is divided into equal contiguous k-block ranges,
+// so some tiles are computed in pieces by several CTAs.  Each piece adds its int32
 // partial sums into a workspace slot with red.add and counts its k-blocks on the
 // slot's counter; the CTA whose count completes the tile reads the slot, runs
 // the epilogue and zeroes the slot again.  Integer addition is exact and
