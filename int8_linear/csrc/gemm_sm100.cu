@@ -311,14 +311,28 @@ __device__ __forceinline__ void epilogue_direct(const GemmArgs &a, const TileCtx
     const int live = min(16, a.N - n0);
     if (wide) {
       uint16_t *o = static_cast<uint16_t *>(a.out) + base;
+      if (a.vec_store && live == 16) {  // 32 bytes of one row: two 16-byte stores
+        uint4 *v = reinterpret_cast<uint4 *>(o);
+        v[0] = make_uint4(bits[0] | (bits[1] << 16), bits[2] | (bits[3] << 16), bits[4] | (bits[5] << 16),
+                          bits[6] | (bits[7] << 16));
+        v[1] = make_uint4(bits[8] | (bits[9] << 16), bits[10] | (bits[11] << 16),
+                          bits[12] | (bits[13] << 16), bits[14] | (bits[15] << 16));
+      } else {
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < live) o[j] = static_cast<uint16_t>(bits[j]);
+        for (int j = 0; j < 16; ++j)
+          if (j < live) o[j] = static_cast<uint16_t>(bits[j]);
+      }
     } else {
       uint32_t *o = static_cast<uint32_t *>(a.out) + base;
+      if (a.vec_store && live == 16) {
+        uint4 *v = reinterpret_cast<uint4 *>(o);
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < live) o[j] = bits[j];
+        for (int q = 0; q < 4; ++q) v[q] = make_uint4(bits[4 * q], bits[4 * q + 1], bits[4 * q + 2], bits[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < live) o[j] = bits[j];
+      }
     }
   }
 }
@@ -1569,9 +1583,11 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
   p->pair = pair ? 1 : 0;
   // Narrow decode tiles: cluster split-K (split 3) on 128 x 256 tiles without swap_ab,
   // for batches of <= 16 tokens: 64-row token tiles, the weight on the MMA's N side.
-  const bool narrow = t.split == 3 && !t.swap_ab;
-  if (narrow && (p->tn != 256 || M > 16))
-    return set_error(I8L_ENOTSUP, "narrow tiles (split 3 without swap_ab) take w_tile 256 and M <= 16");
+  // Split 3 without swap_ab: narrow tiles for batches of <= 16 tokens, else 128-token
+  // tiles with the weight on the MMA's N side and K split over a cluster.
+  const bool narrow = t.split == 3 && !t.swap_ab && M <= 16;
+  if (narrow && p->tn != 256)
+    return set_error(I8L_ENOTSUP, "narrow tiles (split 3 without swap_ab, M <= 16) take w_tile 256");
   p->narrow = narrow ? 1 : 0;
   const int x_rows = narrow ? 64 : kXRows;
   const int max_st = max_stages_for(pair ? p->tn / 2 : p->tn, di.max_smem_optin, x_rows);
@@ -1623,11 +1639,10 @@ static int make_plan(int M, int N, int K, const i8l_tile *user, Plan *p) {
     }
   }
   if (split == 3) {
-    if (!narrow && !t.swap_ab)
-      return set_error(I8L_ENOTSUP, "cluster split-K takes swap_ab tiles or narrow 128 x 256 tiles");
     // Narrow tiles: the leader's operand ring receives (cluster-1) slots of M token rows
-    // x TN int32.  swap_ab tiles: every CTA's ring receives, from each of the other
-    // (cluster-1), the 16-column chunks it owns (one in `cluster`, 128 rows x 16 int32).
+    // x TN int32.  Other tiles (swap_ab, or 128 tokens x TN weight rows): every CTA's ring
+    // receives, from each of the other (cluster-1), the 16-column chunks it owns (one in
+    // `cluster`, 128 rows x 16 int32).
     const long long ring = static_cast<long long>(t.stages) * (x_rows * kBK + p->tn * kBK);
     auto fits = [&](int c) {
       return (narrow ? cluster_recv_bytes(true, M, p->tn, c) : cluster_ring_bytes(p->tn, c)) <= ring;
@@ -1835,7 +1850,10 @@ static int gemm_run(const int8_t *A, int64_t lda, const int8_t *W, int64_t ldw, 
   // Output path: TMA stores through shared memory, or plain stores (cheaper for the
   // few rows of a decode batch).  store: 0 auto, 1 TMA, 2 direct.
   // Narrow tiles always store directly (one warp writes the few token rows).
-  const int store = p.narrow ? 2 : (tile && tile->store ? tile->store : ((swap && M <= 32) ? 2 : 1));
+  // Cluster split-K on 128-token tiles stores directly (each CTA finishes 16-column chunks).
+  const int store = (p.narrow || (p.cluster > 1 && !swap))
+                        ? 2
+                        : (tile && tile->store ? tile->store : ((swap && M <= 32) ? 2 : 1));
   CUtensorMap mo{}, mw{};
   if (aligned_out && store == 1) {
     static const CUtensorMapDataType kTypes[4] = {

@@ -126,9 +126,7 @@ class Config:
             raise NotSupported(f"{self.name}: direct activation loads take swap_ab tiles")
         if self.split == 3 and not 0 <= self.cluster <= 8:
             raise NotSupported(f"{self.name}: clusters hold at most 8 CTAs")
-        if self.split == 3 and not self.swapped and self.bn != 256:
-            raise NotSupported(f"{self.name}: cluster split-K takes swap_ab tiles "
-                               "or narrow 128 x 256 tiles (batches of <= 16 tokens)")
+
         if self.split == 4 and (self.swapped or self.bn != 256):
             raise NotSupported(f"{self.name}: CTA pairs take 128 x 256 tiles without swap_ab")
 

@@ -82,6 +82,8 @@ def candidates(m: int, n: int, k: int, sms: int) -> list[Config]:
         mt = next(t for t in GEMV_TOKENS if t >= m)
         out += [Config(mt, 0, split=5), Config(mt, 0, split=5, ctas=2 * sms),
                 Config(mt, 0, split=5, stages=16)]
+    if 16 < m <= 512:   # cluster split-K with the weight on the MMA's N side (128 tokens x 128/256)
+        out += [Config(128, bn, split=3, cluster=c) for bn in (128, 256) for c in (2, 3, 4, 6, 8)]
     if 64 < m <= 256:   # cluster split-K on the 128- and 256-token swap tiles
         tn = next(t for t in TOKEN_TILES if t >= m)
         out += [Config(tn, 128, swap_ab=True, split=3, cluster=c) for c in (2, 3, 4, 6, 8)]

@@ -194,10 +194,37 @@ def test_narrow_tiles_bit_exact(m, k, n, cluster):
         assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), code)), dt
 
 
-def test_declines_narrow_tiles_for_large_batches():
+def test_split3_without_swap_above_16_tokens_is_a_128_token_cluster_tile():
+    """Split 3 without swap_ab: narrow tiles up to 16 tokens, 128-token tiles with the
+    weight on the MMA's N side and cluster split-K above."""
     a, w = ints((17, 2048), 1), ints((1024, 2048), 2)
-    with pytest.raises(NotSupported, match="narrow"):
-        w8a8_mm(a, w.t(), one(), one(), config=Config(128, 256, split=3, cluster=4))
+    got = w8a8_mm(a, w.t(), one(), one(), raw=True, config=Config(128, 256, split=3, cluster=4))
+    assert np.array_equal(np_(got), exact(a, w))
+
+
+@pytest.mark.parametrize("m", [17, 64, 128, 200, 300])
+@pytest.mark.parametrize("k,n", [(2048, 4096), (6144, 2048), (1040, 1000)])
+@pytest.mark.parametrize("bn,cluster", [(256, 2), (256, 4), (128, 3), (128, 8)])
+def test_cluster_split_on_128_token_tiles(m, k, n, bn, cluster):
+    """Cluster split-K with the tokens on the 128-row MMA side and 128 or 256 weight rows
+    per MMA: each CTA finishes its 16-column chunks (plain stores, 16-byte vectors where
+    the row allows); ragged M, N and K; bf16 with bias and fp32."""
+    a, w = ints((m, k), 400 + m), ints((n, k), 401)
+    g = torch.Generator().manual_seed(402)
+    sa = (torch.rand((m, 1), generator=g) * 1e-2 + 1e-3).cuda()
+    sb = (torch.rand((n, 1), generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    cfg = Config(128, bn, split=3, cluster=cluster)
+    want = exact(a, w)
+    if cluster > (k + 127) // 128:
+        with pytest.raises(NotSupported):
+            w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)
+        return
+    assert np.array_equal(np_(w8a8_mm(a, w.t(), one(), one(), raw=True, config=cfg)), want)
+    got = w8a8_mm(a, w.t(), sa, sb, torch.bfloat16, bias, config=cfg)
+    assert np.array_equal(bits(got), to_bits(og.epilogue_f32(want, np_(sa), np_(sb), np_(bias)), "bf16"))
+    got32 = w8a8_mm(a, w.t(), sa, sb, torch.float32, config=cfg)
+    assert np.array_equal(np_(got32), og.epilogue_f32(want, np_(sa), np_(sb), None))
 
 
 def test_declines_a_cluster_whose_partial_sums_do_not_fit():
