@@ -37,51 +37,6 @@ __device__ __forceinline__ float block_max(float v, float *red) {
   return v;
 }
 
-// block_sum / block_max of two rows at once (one barrier): each row's value goes
-// through exactly the steps the one-row reduction takes, so the results are the same
-// bits.  `red` holds 2 x 32 floats, as `red` above.
-__device__ __forceinline__ void block_sum2(float &a, float &b, float (*red)[32]) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-    b = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, o));
-  }
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-  if (l == 0) {
-    red[0][w] = a;
-    red[1][w] = b;
-  }
-  __syncthreads();
-  a = l < nw ? red[0][l] : 0.f;
-  b = l < nw ? red[1][l] : 0.f;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-    b = __fadd_rn(b, __shfl_xor_sync(0xffffffffu, b, o));
-  }
-}
-
-__device__ __forceinline__ void block_max2(float &a, float &b, float (*red)[32]) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
-  }
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-  if (l == 0) {
-    red[0][w] = a;
-    red[1][w] = b;
-  }
-  __syncthreads();
-  a = l < nw ? red[0][l] : 0.f;
-  b = l < nw ? red[1][l] : 0.f;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
-  }
-}
-
 // block_sum / block_max of R rows at once (one barrier each), every row's value through
 // exactly the one-row reduction's steps.  `red` holds R x 32 floats, as `red` above.
 template <int R, bool kMax>
