@@ -48,8 +48,10 @@ def test_tuned_table_entries_are_valid_tilings():
             for m, entry in buckets.items():
                 cfg = Config(**entry["config"])
                 cfg.check()
-                if cfg.split == 3 and not cfg.swapped:   # narrow tiles take <= 16 tokens
-                    assert int(m) <= 16, (shape, m)
+                if cfg.split == 3 and not cfg.swapped:
+                    # narrow tiles (<= 16 tokens) take 256 weight rows; above 16 tokens the
+                    # same split is the 128-token tile with the weight on the MMA's N side
+                    assert cfg.bm == 128 and (cfg.bn == 256 or int(m) > 16), (shape, m)
                 assert entry.get("graph_us", entry.get("stand_in_us", 0)) > 0
                 count += 1
     assert count > 0
