@@ -53,9 +53,11 @@ extern "C" {
  *                0 = the library's choice; 1 = whole tiles; 2 = stream-K over the SMs,
  *                partial sums reduced through the workspace; 3 = cluster split-K:
  *                the CTAs of a thread-block cluster split one tile's K and reduce over
- *                distributed shared memory (swap_ab tiles of up to 256 tokens: each CTA
- *                finishes one in `cluster` of the tile's 16-column chunks, receiving
- *                them from the others beside a shortened ring; no workspace); 4 = CTA pairs
+ *                distributed shared memory, no workspace: swap_ab tiles of up to 256
+ *                tokens and, without swap_ab above 16 tokens, 128-token tiles of w_tile
+ *                weight rows, each CTA finishing one in `cluster` of the tile's 16-column
+ *                chunks from the others' partial sums (plain stores for the latter);
+ *                without swap_ab at most 16 tokens: narrow tiles, w_tile 256); 4 = CTA pairs
  *                (cta_group::2) on 128 x 256 tiles; 5 = CUDA-core tiles for batches of
  *                at most tok_tile in {1, 2, 4, 8, 16} tokens (w_tile 0, swap_ab 0): each CTA
  *                owns whole output columns (dp4a int8 dot products, no split-K, no

@@ -58,9 +58,10 @@ class Config:
             stream-K over the SMs (reduced in a workspace), 3 cluster split-K (the CTAs
             of a thread-block cluster split a tile's K and reduce over distributed
             shared memory; swap_ab tiles, each CTA finishing one in `cluster` of the
-            tile's 16-column chunks from the others' partial sums, or, without swap_ab, narrow
-            128 x 256 tiles for batches of <= 16 tokens: the weight on the MMA's N side,
-            256 weight rows per MMA instruction), 4 CTA pairs (two SMs
+            tile's 16-column chunks from the others' partial sums; without swap_ab,
+            narrow 128 x 256 tiles for batches of <= 16 tokens, and 128-token tiles of
+            128 or 256 weight rows for larger batches, the weight on the MMA's N side in
+            both), 4 CTA pairs (two SMs
             per 256 x 256 tile with 256-row tcgen05 MMAs; 128 x 256 tiles, no swap_ab),
             5 CUDA-core tiles for decode batches of at most 16 tokens: bm in
             (1, 2, 4, 8, 16) is the most tokens, bn = 0; each CTA owns whole output columns (int8 dot
